@@ -1,0 +1,532 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention backend (one JSON line on rank 0).
+
+Headline workload ("C2"): one GQA decode step per
+sequence - cacheAppend of the new key/value rows, then split-K decode
+attention (gqaScores + gqaSoftmax) over past 4096 cached tokens - for a batch
+of 64 sequences per GPU, Hq 16 / Hkv 4 / head_dim 256, fp16 caches of
+capacity 8192.  The metric is HBM throughput: the logical bytes of the
+step's ops under the reference cost model (lib/GraphIR/Cost.cpp:85-93) per
+second.  Multi-GPU runs shard sequences (weak scaling, no collective).
+
+Keys of the line beyond the base contract:
+  roofline      the decode op (gqaScores + gqaSoftmax launches), timed with
+                CUDA events on its stream, against the measured HBM copy
+                bandwidth of MEASURED_PEAKS.json
+  cpu_baseline  the reference's scalar check code restated in oracle/ (dense
+                fp64 causal GQA), built -O3 -march=native on this host and run
+                with every core on a bounded sample of the same workload
+  e2e           the same step through the C-ABI calls with pinned host
+                buffers: H2D of q and the new rows, D2H of the output, timed
+  secondary     the other kernels of the path on their benchmark configs
+                (C1 prefill, C4 DeltaNet step, C3 DeltaNet prefill)
+`--impl reference` runs the reference arm: the CPU restatement of the
+reference's code (oracle/, "port") on the host cores, same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GQA/DeltaNet attn TFLOP/s (prefill), HBM GB/s (decode) vs roofline, 1-8 GPU"
+C2 = dict(batch=64, past=4096, capacity=8192, query_heads=16, kv_heads=4, head_dim=256)
+FALLBACK_PEAKS = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
+SEED = 179531
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-secondary", action="store_true", help="skip C1/C3/C4 measurements")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+
+
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return dict(hbm_gbs=float(data["hbm_gbs"]), bf16_tflops=float(data["bf16_tflops"]),
+                    bf16_tflops_sustained=float(data.get("bf16_tflops_sustained",
+                                                         data["bf16_tflops"])),
+                    source="measured")
+    return dict(FALLBACK_PEAKS, source="fallback")
+
+
+def profile_traffic(name: str):
+    """DRAM bytes per launch recorded in profiles/<name>.md ('traffic_bytes_per_launch: N')."""
+    path = ROOT / "profiles" / f"{name}.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_id: str):
+        self.index = device_id  # nvidia-smi --id: index or GPU UUID
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+class Dist:
+    def __init__(self, gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg is not None:
+            self.pg.barrier()
+
+    def max(self, value: float) -> float:
+        if self.pg is None:
+            return value
+        import torch
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+def step_bytes(cfg_kinds, tokens, past, capacity, batch, **shape):
+    """Logical bytes and MACs of one step of the given layers (reference cost model)."""
+    import llminfer_b200 as L
+    cfg, keep = L.make_stack_config(cfg_kinds, 1, capacity, **shape)
+    d = json.loads(L.describe_step(cfg, tokens, past))
+    per_op = {}
+    for op in d["ops"]:
+        c = op["cost"]
+        per_op.setdefault(op["kind"], [0, 0, 0])
+        per_op[op["kind"]][0] += (c["logical_read_bytes"] + c["logical_write_bytes"]) * batch
+        per_op[op["kind"]][1] += c["fp_macs"] * batch
+    return per_op
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port, every core)
+
+
+def native_oracle():
+    import importlib
+    sys.path.insert(0, str(ROOT / "tests"))
+    oracle = importlib.import_module("_oracle")
+    out = Path(tempfile.gettempdir()) / f"llmi_oracle_native_{os.getpid()}.so"
+    try:
+        subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "native",
+                        f"NATIVE_OUT={out}"], check=True, capture_output=True)
+        lib = oracle.load(out)
+        flags = "-O3 -march=native"
+    except (subprocess.CalledProcessError, OSError):
+        lib = oracle.load()
+        flags = "-O3"
+    oracle._lib = lib
+    return oracle, flags
+
+
+def cpu_decode_sample(q, kc, vc, past, target_s=12.0, max_seqs=None):
+    """Times the dense fp64 oracle on n sequences of the decode workload, n chosen so the
+    sample takes about target_s.  Returns (GB/s, seconds, n, threads, flags)."""
+    import numpy as np
+    oracle, flags = native_oracle()
+    threads = oracle.lib().oracle_max_threads()
+    max_seqs = q.shape[0] if max_seqs is None else max_seqs
+    rows = past + 1
+
+    def host(n):
+        return (q[:n].cpu().numpy(), kc[:n, :rows].cpu().numpy(), vc[:n, :rows].cpu().numpy())
+
+    qs, ks, vs = host(1)
+    t0 = time.perf_counter()
+    oracle.gqa_dense(qs, ks, vs, past, threads=threads)
+    one = time.perf_counter() - t0
+    n = int(max(1, min(max_seqs, round(target_s / max(one, 1e-6)))))
+    qs, ks, vs = host(n)
+    t0 = time.perf_counter()
+    oracle.gqa_dense(qs, ks, vs, past, threads=threads)
+    secs = time.perf_counter() - t0
+    per_seq = step_bytes([1], 1, past, C2["capacity"], 1, query_heads=C2["query_heads"],
+                         kv_heads=C2["kv_heads"], head_dim=C2["head_dim"])["CausalGqa"][0]
+    del np
+    return per_seq * n / secs / 1e9, secs, n, threads, flags
+
+
+# ---------------------------------------------------------------------------
+# our arm
+
+
+def decode_inputs(torch, device, seed):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    B, P, CAP = C2["batch"], C2["past"], C2["capacity"]
+    Hq, Hkv, D = C2["query_heads"], C2["kv_heads"], C2["head_dim"]
+    kc = torch.zeros(B, CAP, Hkv, D, dtype=torch.float16, device=device)
+    vc = torch.zeros_like(kc)
+    kc[:, :P].normal_(generator=g)
+    vc[:, :P].normal_(generator=g)
+    q = torch.randn(B, 1, Hq, D, generator=g, device=device).half()
+    kn = torch.randn(B, 1, Hkv, D, generator=g, device=device).half()
+    vn = torch.randn(B, 1, Hkv, D, generator=g, device=device).half()
+    return q, kn, vn, kc, vc
+
+
+def run_ours(args, dist):
+    import torch
+
+    from llminfer_b200 import ops
+
+    device = torch.device("cuda", dist.local)
+    torch.cuda.set_device(device)
+    peaks = load_peaks()
+    P = C2["past"]
+    q, kn, vn, kc, vc = decode_inputs(torch, device, SEED + dist.rank)
+    out = torch.empty_like(q)
+    ws = torch.empty(ops.decode_workspace_bytes(C2["batch"], C2["query_heads"], C2["kv_heads"],
+                                                C2["head_dim"], P), dtype=torch.uint8,
+                     device=device)
+
+    def step():
+        ops.cache_append(kn, kc, P)
+        ops.cache_append(vn, vc, P)
+        ops.gqa_decode(q, kc, vc, P, out=out, workspace=ws)
+
+    costs = step_bytes([1], 1, P, C2["capacity"], C2["batch"], query_heads=C2["query_heads"],
+                       kv_heads=C2["kv_heads"], head_dim=C2["head_dim"])
+    bytes_step = costs["KvAppend"][0] + costs["CausalGqa"][0]
+    bytes_decode = costs["CausalGqa"][0]
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+    except (AttributeError, RuntimeError):
+        gpu_id = str(device.index)
+    with ClockSampler(gpu_id) as clocks:
+        start.record()
+        for i in range(K):
+            ops.cache_append(kn, kc, P)
+            ops.cache_append(vn, vc, P)
+            ev[i][0].record()
+            ops.gqa_decode(q, kc, vc, P, out=out, workspace=ws)
+            ev[i][1].record()
+        end.record()
+        torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ops.poll_error()
+    ms = dist.max(start.elapsed_time(end))
+    decode_ms = dist.max(statistics.mean(a.elapsed_time(b) for a, b in ev))
+    ms_step = ms / K
+    value = bytes_step * dist.world * K / (ms / 1e3) / 1e9
+    achieved = bytes_decode / (decode_ms / 1e3) / 1e9
+    traffic = profile_traffic("gqa_decode_c2")
+
+    # End to end through the C-ABI calls with pinned host buffers.
+    hq = torch.empty(q.shape, dtype=q.dtype, pin_memory=True).copy_(q.cpu())
+    hk = torch.empty(kn.shape, dtype=kn.dtype, pin_memory=True).copy_(kn.cpu())
+    hv = torch.empty(vn.shape, dtype=vn.dtype, pin_memory=True).copy_(vn.cpu())
+    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        ops.cache_append(dk, kc, P)
+        ops.cache_append(dv, vc, P)
+        ops.gqa_decode(dq, kc, vc, P, out=out, workspace=ws)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(K):
+        e2e_step()
+    e2.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e2e_ms = dist.max(s2.elapsed_time(e2))
+    h2d = (q.numel() + kn.numel() + vn.numel()) * 2
+    d2h = out.numel() * 2
+
+    secondary = []
+    if not args.no_secondary and dist.world == 1:
+        secondary = run_secondary(torch, ops, device, peaks)
+
+    cpu = None
+    if not args.no_cpu and dist.world == 1 and dist.rank == 0:
+        gbs, secs, n, threads, flags = cpu_decode_sample(q, kc, vc, P)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"{n} of 64 sequences of the C2 decode step (CausalGqa), "
+                         f"{secs:.1f} s; dense fp64 check of tests/FlashAttentionTest.mm:53-85 "
+                         f"restated in oracle/oracle.c, gcc {flags} -fopenmp"}
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": dist.world,
+        "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic: seeded N(0,1) fp16 (torch Philox on device), per-rank seed",
+        "config": {
+            "workload": "C2 GQA decode step (cacheAppend x2 + gqaScores + gqaSoftmax): batch 64 "
+                        "per GPU, 1 new token, past 4096, capacity 8192, Hq 16, Hkv 4, D 256, "
+                        "fp32 softmax/accumulation",
+            "global_batch": C2["batch"] * dist.world, "past": P, "capacity": C2["capacity"],
+            "query_heads": C2["query_heads"], "kv_heads": C2["kv_heads"],
+            "head_dim": C2["head_dim"],
+            "parallelism": f"sequence-sharded over {dist.world} GPU(s), no collective",
+            "l2": "no flush: each step streams 2.15 GB of KV cache, far above the 126 MB L2",
+            "bytes_per_step_per_gpu": bytes_step,
+        },
+        "roofline": {"kernel": "gqaScores+gqaSoftmax (decode op)", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                     "peak_source": peaks["source"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                     "algorithmic_bytes_per_launch": bytes_decode,
+                     "avg_launch_ms": round(decode_ms, 4)},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(bytes_step * dist.world * K / (e2e_ms / 1e3) / 1e9, 2),
+                "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms / K, 4)},
+        "gpu_launches": 4 * K,
+        "clocks": clocks.summary(),
+        "secondary": secondary,
+    }
+    return line
+
+
+def time_op(torch, fn, reps=10, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(reps)]
+    for a, b in evs:
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    t = sorted(a.elapsed_time(b) for a, b in evs)
+    return statistics.median(t), t[0]
+
+
+def run_secondary(torch, ops, device, peaks):
+    """The other kernels of the path on their benchmark configs (CUDA events, median)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED)
+    res = []
+    # C1: GQA prefill, B=1, T=128, past 0.
+    q = torch.randn(1, 128, 16, 256, generator=g, device=device).half()
+    kc = torch.randn(1, 128, 4, 256, generator=g, device=device).half()
+    vc = torch.randn(1, 128, 4, 256, generator=g, device=device).half()
+    out = torch.empty_like(q)
+    med, best = time_op(torch, lambda: ops.gqa_prefill(q, kc, vc, 0, out=out))
+    macs = step_bytes([1], 128, 0, 128, 1, query_heads=16, kv_heads=4, head_dim=256)["CausalGqa"][1]
+    tf = 2 * macs / (med / 1e3) / 1e12
+    res.append({"workload": "C1 GQA prefill B=1 T=128 past 0 (gqaFlashAttention)",
+                "ms": round(med, 4), "value": round(tf, 3), "unit": "TFLOP/s",
+                "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4)})
+    # C4: DeltaNet recurrent step, B=256.
+    B, Hk, dk, Hv, dv = 256, 16, 128, 32, 128
+    qd = torch.nn.functional.normalize(torch.randn(B, 1, Hk, dk, generator=g, device=device), dim=-1)
+    qd = (qd / dk ** 0.5).reshape(B, 1, Hk * dk).contiguous()
+    kd = torch.nn.functional.normalize(torch.randn(B, 1, Hk, dk, generator=g, device=device), dim=-1)
+    kd = kd.reshape(B, 1, Hk * dk).contiguous()
+    vd = torch.randn(B, 1, Hv * dv, generator=g, device=device).half()
+    beta = torch.sigmoid(torch.randn(B, 1, Hv, generator=g, device=device)).half().float()
+    decay = torch.exp(-torch.nn.functional.softplus(torch.randn(B, 1, Hv, generator=g, device=device)))
+    state = torch.randn(B, Hv, dk, dv, generator=g, device=device) * 0.02
+    od = torch.empty_like(vd)
+    med, best = time_op(torch, lambda: ops.delta_update(qd, kd, vd, beta, decay, state, out=od))
+    nbytes = step_bytes([0], 1, 0, 1, B, key_heads=Hk, key_dim=dk, value_heads=Hv,
+                        value_dim=dv)["DeltaUpdate"][0]
+    gbs = nbytes / (med / 1e3) / 1e9
+    res.append({"workload": "C4 DeltaNet recurrent step B=256 (graphDeltaUpdate)",
+                "ms": round(med, 4), "value": round(gbs, 1), "unit": "GB/s",
+                "frac_of_hbm_peak": round(gbs / peaks["hbm_gbs"], 4)})
+    del qd, kd, vd, beta, decay, state, od
+    # C3: DeltaNet prefill, B=4, T=4096.
+    B, T = 4, 4096
+    qd = torch.nn.functional.normalize(torch.randn(B, T, Hk, dk, generator=g, device=device), dim=-1)
+    qd = (qd / dk ** 0.5).reshape(B, T, Hk * dk).contiguous()
+    kd = torch.nn.functional.normalize(torch.randn(B, T, Hk, dk, generator=g, device=device), dim=-1)
+    kd = kd.reshape(B, T, Hk * dk).contiguous()
+    vd = torch.randn(B, T, Hv * dv, generator=g, device=device).half()
+    beta = torch.sigmoid(torch.randn(B, T, Hv, generator=g, device=device)).half().float()
+    decay = torch.exp(-torch.nn.functional.softplus(torch.randn(B, T, Hv, generator=g, device=device)))
+    state = torch.zeros(B, Hv, dk, dv, device=device)
+    od = torch.empty_like(vd)
+    med, best = time_op(torch, lambda: ops.delta_update(qd, kd, vd, beta, decay, state, out=od),
+                        reps=3, warmup=1)
+    cost = step_bytes([0], T, 0, T, B, key_heads=Hk, key_dim=dk, value_heads=Hv,
+                      value_dim=dv)["DeltaUpdate"]
+    res.append({"workload": "C3 DeltaNet prefill B=4 T=4096 (graphDeltaUpdate)",
+                "ms": round(med, 4), "value": round(cost[0] / (med / 1e3) / 1e9, 1),
+                "unit": "GB/s", "tflops_cost_model": round(2 * cost[1] / (med / 1e3) / 1e12, 3),
+                "frac_of_hbm_peak": round(cost[0] / (med / 1e3) / 1e9 / peaks["hbm_gbs"], 4)})
+    return res
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+
+
+def run_reference(args, dist):
+    import numpy as np
+    if dist.rank != 0:
+        return None
+    sys.path.insert(0, str(ROOT / "tests"))
+    import _inputs
+    oracle, flags = native_oracle()
+    threads = oracle.lib().oracle_max_threads()
+    P = C2["past"]
+    # One step = a bounded sample of the C2 decode workload: n sequences.
+    q, k, v = _inputs.gqa_case(1, 1, P, C2["query_heads"], C2["kv_heads"], C2["head_dim"],
+                               seed=SEED)
+    t0 = time.perf_counter()
+    oracle.gqa_dense(q, k, v, P, threads=threads)
+    one = time.perf_counter() - t0
+    n = int(max(1, min(C2["batch"], round(1.5 / max(one, 1e-6)))))
+    qs = np.repeat(q, n, axis=0)
+    ks = np.repeat(k, n, axis=0)
+    vs = np.repeat(v, n, axis=0)
+    per_seq = step_bytes([1], 1, P, C2["capacity"], 1, query_heads=C2["query_heads"],
+                         kv_heads=C2["kv_heads"], head_dim=C2["head_dim"])
+    bytes_seq = per_seq["KvAppend"][0] + per_seq["CausalGqa"][0]
+    for _ in range(args.warmup):
+        oracle.gqa_dense(qs[:1], ks[:1], vs[:1], P, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.gqa_dense(qs, ks, vs, P, threads=threads)
+        times.append(time.perf_counter() - t0)
+    secs = sum(times)
+    value = bytes_seq * n * args.steps / secs / 1e9
+    sample = (f"{n} of the 64 sequences of the C2 decode step per timed step, dense fp64 causal "
+              f"GQA (tests/FlashAttentionTest.mm:53-85 restated in oracle/oracle.c, gcc {flags} "
+              f"-fopenmp); the reference's own path is Metal and cannot run here")
+    return {
+        "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "impl": "reference",
+        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(secs / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic: seeded N(0,1) fp16 (numpy Philox)",
+        "config": {"workload": "C2 GQA decode step, bounded sample (see cpu_baseline.sample)",
+                   "global_batch": C2["batch"], "past": P, "capacity": C2["capacity"],
+                   "query_heads": C2["query_heads"], "kv_heads": C2["kv_heads"],
+                   "head_dim": C2["head_dim"], "parallelism": "host cores (OpenMP)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+
+
+def main():
+    args = parse_args()
+    dist = Dist(args.gpus)
+    try:
+        if args.impl == "reference":
+            line = run_reference(args, dist)
+        else:
+            line = run_ours(args, dist)
+        if dist.rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

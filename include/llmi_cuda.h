@@ -1,0 +1,235 @@
+/*
+ * llmi_cuda.h — C ABI of the B200 (sm_100a) attention backend for llminfer.
+ *
+ * These entry points replace, one for one, the Metal kernels that llminfer's
+ * backend lowering dispatches for the attention ops of the Qwen3.5 hybrid
+ * backbone (lib/Backend/Metal/MetalExecutionPlan.cpp:511-549 for
+ * KvAppend/CausalGqa, :663-676 for DeltaUpdate).  The parameter structs keep
+ * the field order and meaning of the reference's POD structs, so a CUDA
+ * sibling of the lowering fills them exactly as the Metal lowering does.
+ *
+ * Conventions shared by every call:
+ *  - All tensor pointers are DEVICE pointers owned by the caller (the
+ *    executor); no call allocates, frees or retains them.  fp16 tensors are
+ *    passed as uint16_t bit patterns (IEEE binary16).
+ *  - `stream` is a cudaStream_t (NULL = the legacy default stream).  Calls are
+ *    stream-ordered and do not synchronise; calls on different streams may run
+ *    concurrently when they touch disjoint buffers.
+ *  - The return value is an llmi_status.  On failure llmi_cuda_last_error()
+ *    returns a message for the calling thread.  Argument errors are reported
+ *    before anything is launched, so buffers are untouched (the reference's
+ *    "failure before submit leaves the state untouched",
+ *    lib/Backend/Metal/MetalExecutor.mm:285-287).
+ *  - `batch` sequences are processed per call; sequence s of a tensor starts
+ *    at element s * <stride> (cache strides are in elements).  Every sequence
+ *    of a call shares the step shape (tokens, past), like one llminfer step.
+ *  - There is no CPU fallback: shapes the CUDA kernels do not implement
+ *    return LLMI_UNSUPPORTED.
+ */
+#ifndef LLMI_CUDA_H
+#define LLMI_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  LLMI_OK = 0,
+  LLMI_INVALID_ARGUMENT = 1,  /* rejected before launch; buffers untouched */
+  LLMI_UNSUPPORTED = 2,       /* valid op, shape outside the CUDA kernels */
+  LLMI_CUDA_ERROR = 3,        /* a CUDA runtime call failed */
+  LLMI_DEVICE_TIMEOUT = 4,    /* a bounded device-side wait gave up */
+  LLMI_WORKSPACE_TOO_SMALL = 5,
+  LLMI_SESSION_INVALID = 6,   /* session poisoned by a failure after launch */
+  LLMI_CAPACITY_EXCEEDED = 7  /* chunk does not fit capacity - past */
+} llmi_status;
+
+/* CacheParams (lib/Backend/Metal/Kernels/ReferenceParams.h:49-51):
+ * `count` fp16 elements copied to element `offset` of each sequence's cache. */
+typedef struct {
+  unsigned count, offset;
+} llmi_cache_params;
+
+/* GqaParams (lib/Backend/Metal/Kernels/ReferenceParams.h:53-55). */
+typedef struct {
+  unsigned tokens, queryHeads, kvHeads, headDim, past;
+} llmi_gqa_params;
+
+/* GraphDeltaParams (lib/Backend/Metal/Kernels/GraphParams.h:50-52). */
+typedef struct {
+  unsigned tokens, keyHeads, keyDim, valueHeads, valueDim;
+} llmi_delta_params;
+
+/* Message of the calling thread's last failure ("" after success). */
+const char *llmi_cuda_last_error(void);
+/* Stable name of a status code, e.g. "LLMI_UNSUPPORTED". */
+const char *llmi_cuda_status_name(int status);
+
+/* cacheAppend (lib/Backend/Metal/Kernels/Reference.metal:295-301, lowered at
+ * MetalExecutionPlan.cpp:516-522, once for keys and once for values):
+ *   cache[s*cache_stride + p->offset + i] = input[s*input_stride + i]
+ * for i < p->count and s < batch.  `input` rows are the step's new keys (or
+ * values) [tokens][kvHeads][headDim]; offset = past*kvHeads*headDim. */
+int llmi_cuda_cache_append(const llmi_cache_params *p, unsigned batch,
+                           const uint16_t *input, size_t input_stride,
+                           uint16_t *cache, size_t cache_stride, void *stream);
+
+/* CausalGqa with tokens > 1: gqaFlashAttention
+ * (lib/Backend/Metal/Kernels/FlashAttention.metal:1-83).
+ *   q, out:  [batch][tokens][queryHeads][headDim] fp16, dense
+ *   k_cache, v_cache: per sequence [capacity][kvHeads][headDim] fp16 at
+ *            sequence stride cache_stride; rows [0, past+tokens) are read
+ * Query token t attends to keys [0, past+t]; q head h reads kv head
+ * h / (queryHeads/kvHeads); scores are scaled by 1/sqrt(headDim); softmax and
+ * accumulation in fp32, output rounded to fp16.  Any tokens >= 1 is accepted. */
+int llmi_cuda_gqa_prefill(const llmi_gqa_params *p, unsigned batch,
+                          const uint16_t *q, const uint16_t *k_cache,
+                          const uint16_t *v_cache, size_t cache_stride,
+                          uint16_t *out, void *stream);
+
+/* Bytes of device scratch llmi_cuda_gqa_decode needs for this shape on the
+ * current device (0 on error; see llmi_cuda_last_error). */
+size_t llmi_cuda_gqa_decode_workspace(const llmi_gqa_params *p, unsigned batch);
+
+/* CausalGqa with tokens == 1: the reference's gqaScores / gqaSoftmax /
+ * gqaValue dispatches (Reference.metal:303-323, Graph.metal:172-230,
+ * lowered at MetalExecutionPlan.cpp:536-548), done as split-K flash decoding:
+ * a partial-softmax pass over slices of the cache writes (max, sum, partial
+ * output) records into `workspace`, and a merge pass combines them and writes
+ * fp16 `out`.  Same layouts and semantics as llmi_cuda_gqa_prefill with
+ * tokens == 1.  workspace_bytes must be at least
+ * llmi_cuda_gqa_decode_workspace(p, batch). */
+int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch,
+                         const uint16_t *q, const uint16_t *k_cache,
+                         const uint16_t *v_cache, size_t cache_stride,
+                         uint16_t *out, void *workspace,
+                         size_t workspace_bytes, void *stream);
+
+/* DeltaUpdate: graphDeltaUpdate (lib/Backend/Metal/Kernels/Graph.metal:146-170
+ * with updateDeltaColumn, Reference.metal:182-197; operand contract
+ * lib/GraphIR/Graph.cpp:226-246).  Per sequence:
+ *   q, k:   [tokens][keyHeads*keyDim] fp32
+ *   v:      [tokens][valueHeads*valueDim] fp16
+ *   beta, decay: [tokens][valueHeads] fp32
+ *   state:  [valueHeads][keyDim][valueDim] fp32, read and written in place
+ *   out:    [tokens][valueHeads*valueDim] fp16
+ * For each token: S = decay*S; pred = S^T k; delta = beta*(v - pred);
+ * S += k delta^T; y = S^T q.  Value head vh uses key head
+ * vh / (valueHeads/keyHeads).  tokens == 1 runs the register-resident
+ * recurrent step; tokens > 1 runs the chunked (chunk 64) form. */
+int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch,
+                           const float *q, const float *k, const uint16_t *v,
+                           const float *beta, const float *decay, float *state,
+                           uint16_t *out, void *stream);
+
+/* Synchronises `stream`, then reads and clears the device error word that
+ * kernels set when a bounded wait gives up.  Returns LLMI_OK,
+ * LLMI_DEVICE_TIMEOUT or LLMI_CUDA_ERROR (for an asynchronous launch or
+ * execution error).  The reference's equivalent check is the non-finite flag
+ * read after each step (MetalExecutor.mm:180-187). */
+int llmi_cuda_poll_error(void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Attention-stack session: the CUDA counterpart of MetalSession
+ * (include/llminfer/Backend/Metal/MetalSession.h:28-44) reduced to the
+ * attention ops.  It owns the per-layer state buffers (KV caches
+ * [batch][capacity][kvHeads][headDim] fp16, recurrent states
+ * [batch][valueHeads][keyDim][valueDim] fp32), keeps `past`, lowers each
+ * step's ops to kernels with the reference's --plan names and runs them on
+ * its stream. */
+
+typedef struct llmi_session llmi_session;
+
+enum { LLMI_LAYER_DELTANET = 0, LLMI_LAYER_GQA = 1 };
+
+typedef struct {
+  unsigned layers;
+  const unsigned char *layer_kinds; /* layers entries of LLMI_LAYER_* */
+  unsigned batch, capacity;
+  unsigned queryHeads, kvHeads, headDim;            /* GQA layers */
+  unsigned keyHeads, keyDim, valueHeads, valueDim;  /* DeltaNet layers */
+} llmi_stack_config;
+
+/* One layer's step operands (device pointers, dense, batch-major).
+ *   GQA:      q f16 [B][T][Hq][D], k/v f16 [B][T][Hkv][D] (appended to the
+ *             caches at rows [past, past+T)), out f16 [B][T][Hq][D]
+ *   DeltaNet: q/k f32 [B][T][Hk*dk], v f16 [B][T][Hv*dv],
+ *             beta/decay f32 [B][T][Hv], out f16 [B][T][Hv*dv] */
+typedef struct {
+  const void *q, *k, *v;
+  const float *beta, *decay;
+  void *out;
+} llmi_layer_io;
+
+enum { LLMI_STATE_KEYS = 0, LLMI_STATE_VALUES = 1, LLMI_STATE_RECURRENT = 2 };
+
+/* Allocates and zeroes the states (MetalExecutor::initialize,
+ * MetalExecutor.mm:56-94) on the current device; `stream` is borrowed. */
+int llmi_cuda_session_open(const llmi_stack_config *config, void *stream,
+                           llmi_session **session);
+void llmi_cuda_session_close(llmi_session *session);
+
+/* MetalSession::step (MetalExecutor.mm:255-292) for the attention ops: checks
+ * 1 <= tokens <= capacity - past, lowers and launches every layer in order,
+ * waits, checks the device error word, and advances past by tokens only on
+ * success.  A failure after launch marks the session invalid until reset.
+ * `io` has one entry per layer.  With trace_plan != 0 the dispatches are
+ * recorded for llmi_cuda_session_plan. */
+int llmi_cuda_session_step(llmi_session *session, unsigned tokens,
+                           const llmi_layer_io *io, int trace_plan);
+
+/* Like session_step but does not wait or poll: the work is only enqueued on
+ * the session stream, and past advances when the launches were accepted.
+ * For timed loops and CUDA-graph capture; follow with
+ * llmi_cuda_session_sync before trusting the results. */
+int llmi_cuda_session_enqueue(llmi_session *session, unsigned tokens,
+                              const llmi_layer_io *io);
+/* Waits for the session stream and checks the device error word; on failure
+ * the session becomes invalid. */
+int llmi_cuda_session_sync(llmi_session *session);
+
+/* MetalSession::reset (MetalExecutor.mm:294-298): zero all states, past = 0,
+ * clear the invalid mark. */
+int llmi_cuda_session_reset(llmi_session *session);
+uint64_t llmi_cuda_session_past(const llmi_session *session);
+int llmi_cuda_session_is_invalid(const llmi_session *session);
+
+/* Device pointer and size of one state buffer of `layer`
+ * (which = LLMI_STATE_*). */
+int llmi_cuda_session_state(llmi_session *session, unsigned layer,
+                            unsigned which, void **pointer, size_t *bytes);
+
+/* Copies `bytes` bytes between a state buffer of `layer` and caller device
+ * memory, ordered on the session stream (read: state -> dst, write:
+ * src -> state), then waits.  bytes must equal the state's size.  Used to
+ * seed recurrent states and to inspect caches and states. */
+int llmi_cuda_session_read_state(llmi_session *session, unsigned layer,
+                                 unsigned which, void *dst, size_t bytes);
+int llmi_cuda_session_write_state(llmi_session *session, unsigned layer,
+                                  unsigned which, const void *src,
+                                  size_t bytes);
+
+/* The last traced step's dispatches as JSON lines
+ * {"op_index":i,"kernel":"...","layer":l} — the records llmi-run --plan prints
+ * (tools/run/Main.cpp:244-255).  Copies at most len-1 bytes plus a NUL and
+ * returns the full length. */
+size_t llmi_cuda_session_plan(const llmi_session *session, char *buffer,
+                              size_t len);
+
+/* Host-only lowering of one step (no GPU needed): JSON with the step, each
+ * op's kind, layer, state effects and logical cost (the `llmi graph --json`
+ * fields of tools/modelconverter/GraphCommand.cpp:82-146 for these ops), and
+ * the dispatches the CUDA backend would launch.  Returns the full length
+ * (0 on error, with *status set). */
+size_t llmi_cuda_describe_step(const llmi_stack_config *config,
+                               unsigned tokens, uint64_t past, char *buffer,
+                               size_t len, int *status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,377 @@
+// Decode attention (CausalGqa with one new token per sequence) as split-K
+// flash decoding.
+//
+// The reference computes decode in three dispatches with an fp16 score
+// buffer [tokens*queryHeads, past+tokens]: gqaScores
+// (Reference.metal:303-323), gqaSoftmax (Graph.metal:172-210) and gqaValue
+// (Graph.metal:212-230).  Here the cache is streamed exactly once:
+//
+//  * The key range of every (sequence, kv head) "unit" is cut into tiles of
+//    16 keys, and the tiles of all units are laid end to end and divided
+//    evenly among "workers" (warps).  A worker streams its tiles through its
+//    own bulk-copy pipeline, keeps an online softmax for the GQA group of its
+//    unit, and writes one partial record (max, sum, unnormalised output) for
+//    every unit it touches.  Because whole tiles are balanced across warps,
+//    every SM streams the same number of bytes whatever the batch and
+//    context length.
+//  * The merge pass combines the records of each unit (log-sum-exp) and
+//    writes the fp16 output.
+//
+// Scores and the softmax stay in fp32 (log2 domain).  Probabilities enter the
+// P.V product rounded to fp16, as in the reference's decode path.
+//
+// Tensor-core mapping of one 16-key tile (m16n8k16, f16 x f16 -> f32):
+//   S^T[key][head]  = K[key][:] . Q[head][:]       A = K tile (ldmatrix),
+//                                                   B = Q (registers), N = 8
+//   O^T[d][head]   += V^T[d][key] . P^T[key][head] A = V tile (ldmatrix.trans),
+//                                                   B = P via movmatrix.trans
+// so the group's query heads (<= 8) sit in N and no row of M is wasted.
+#pragma once
+
+#include "common.cuh"
+
+namespace llmi {
+namespace decode {
+
+constexpr int kTileKeys = 16;
+
+// How the key tiles of all units are divided among workers.  Worker w owns
+// tiles [w*tiles_per_worker, (w+1)*tiles_per_worker) of the concatenation of
+// the units' tile lists and writes one record per unit it touches.
+struct Partition {
+  uint32_t units;             // batch * kvHeads
+  uint32_t tiles_per_unit;    // key tiles (or key splits) per unit
+  uint32_t tiles_per_worker;
+  uint32_t max_span;          // records reserved per worker
+  uint32_t workers;
+};
+
+__host__ __device__ inline uint32_t first_unit(const Partition &pt, uint32_t worker) {
+  return uint32_t((uint64_t(worker) * pt.tiles_per_worker) / pt.tiles_per_unit);
+}
+
+__host__ __device__ inline uint64_t record_index(const Partition &pt, uint32_t worker,
+                                                 uint32_t unit) {
+  return uint64_t(worker) * pt.max_span + (unit - first_unit(pt, worker));
+}
+
+// Record layout (fp32): [max: G][sum: G][out: G][D], padded to 4 floats.
+__host__ __device__ inline uint32_t record_floats(uint32_t group, uint32_t head_dim) {
+  return (2 * group + group * head_dim + 3) & ~3u;
+}
+
+struct Args {
+  const __half *q;       // [batch][queryHeads][D]  (tokens == 1)
+  const __half *k, *v;   // caches, sequence stride cache_stride
+  size_t cache_stride;
+  __half *out;           // [batch][queryHeads][D]
+  float *records;
+  Partition pt;
+  uint32_t kv_heads, group, head_dim, keys;  // keys = past + 1
+  uint32_t record_floats;
+  float scale_log2;      // log2(e) / sqrt(D)
+};
+
+template <int D, int WARPS, int STAGES>
+struct MmaShape {
+  static constexpr int kRowBytes = D * 2;
+  static constexpr int kRowStride = D * 2 + 16;  // +16 B: conflict-free ldmatrix
+  static constexpr int kTileBytes = kTileKeys * kRowStride;
+  static constexpr int kStageBytes = 2 * kTileBytes;  // K tile + V tile
+  static constexpr int kSmemBytes = WARPS * STAGES * kStageBytes + WARPS * STAGES * 8;
+};
+
+// Partial pass on tensor cores.  One CTA per SM; each warp is a worker with a
+// private STAGES-deep pipeline of 16-key tiles.  Requires D % 16 == 0,
+// D <= 256 and group <= 8.
+template <int D, int WARPS, int STAGES>
+__global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
+  using Shape = MmaShape<D, WARPS, STAGES>;
+  constexpr int KS = D / 16;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t *stages = smem + warp * STAGES * Shape::kStageBytes;
+  uint64_t *bars =
+      reinterpret_cast<uint64_t *>(smem + WARPS * STAGES * Shape::kStageBytes) + warp * STAGES;
+
+  const Partition pt = a.pt;
+  const uint32_t worker = blockIdx.x * WARPS + warp;
+  const uint32_t total = pt.units * pt.tiles_per_unit;
+  const uint32_t begin = min(total, worker * pt.tiles_per_worker);
+  const uint32_t end = min(total, begin + pt.tiles_per_worker);
+  if (begin >= end)
+    return;  // warps are independent: no CTA-wide barrier below
+
+  if (lane == 0) {
+    for (int s = 0; s < STAGES; ++s)
+      mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+
+  const uint64_t policy = policy_evict_first();
+  const uint32_t tpu = pt.tiles_per_unit;
+
+  // Lanes 0-15 fetch the 16 key rows, lanes 16-31 the 16 value rows.  Rows
+  // past the end of the cache range repeat the last valid row (their scores
+  // are masked to -inf, so they contribute exactly zero).
+  auto issue = [&](uint32_t tile, int stage) {
+    const uint32_t unit = tile / tpu, key0 = (tile % tpu) * kTileKeys;
+    const uint32_t seq = unit / a.kv_heads, kvh = unit % a.kv_heads;
+    const uint32_t valid = min(uint32_t(kTileKeys), a.keys - key0);
+    if (lane == 0)
+      mbar_arrive_expect_tx(&bars[stage], 2 * kTileKeys * Shape::kRowBytes);
+    __syncwarp();
+    const uint32_t row = lane & 15;
+    const uint32_t key = key0 + min(row, valid - 1);
+    const __half *src = (lane < 16 ? a.k : a.v) + seq * a.cache_stride +
+                        (size_t(key) * a.kv_heads + kvh) * D;
+    uint8_t *dst = stages + stage * Shape::kStageBytes + (lane < 16 ? 0 : Shape::kTileBytes) +
+                   row * Shape::kRowStride;
+    bulk_g2s(dst, src, Shape::kRowBytes, &bars[stage], policy);
+  };
+
+  for (int s = 0; s < STAGES; ++s)
+    if (begin + s < end)
+      issue(begin + s, s);
+
+  const uint32_t head0 = (lane & 3) * 2;  // this lane's two heads (N columns)
+  const uint32_t krow = lane >> 2;        // this lane's key rows: krow, krow+8
+  uint32_t unit = 0xffffffffu;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float o[KS][4];
+  uint32_t qf[KS][2];
+
+  auto flush = [&](uint32_t u) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 4);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 8);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 16);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 4);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 8);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 16);
+    float *rec = a.records + record_index(pt, worker, u) * a.record_floats;
+    const uint32_t G = a.group;
+    if (lane < 4) {
+      if (head0 < G) {
+        rec[head0] = m0;
+        rec[G + head0] = l0;
+      }
+      if (head0 + 1 < G) {
+        rec[head0 + 1] = m1;
+        rec[G + head0 + 1] = l1;
+      }
+    }
+    float *out0 = rec + 2 * G + head0 * D;
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+      const uint32_t d = mt * 16 + krow;
+      if (head0 < G) {
+        out0[d] = o[mt][0];
+        out0[d + 8] = o[mt][2];
+      }
+      if (head0 + 1 < G) {
+        out0[D + d] = o[mt][1];
+        out0[D + d + 8] = o[mt][3];
+      }
+    }
+  };
+
+  const uint32_t k_lane = ((lane & 7) + ((lane >> 3) & 1) * 8) * Shape::kRowStride + (lane >> 4) * 16;
+  const uint32_t v_lane = ((lane & 7) + (lane >> 4) * 8) * Shape::kRowStride + ((lane >> 3) & 1) * 16;
+
+  uint32_t t = begin;
+  bool ok = true;
+  for (; t < end; ++t) {
+    const uint32_t j = t - begin;
+    const int stage = j % STAGES;
+    const uint32_t u = t / tpu;
+    if (u != unit) {
+      if (unit != 0xffffffffu)
+        flush(unit);
+      unit = u;
+      const uint32_t seq = u / a.kv_heads, kvh = u % a.kv_heads;
+      const uint32_t head = lane >> 2;  // B operand column n = lane/4
+      const __half *qrow = a.q + (size_t(seq) * a.kv_heads * a.group + kvh * a.group + head) * D;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        if (head < a.group) {
+          qf[ks][0] = *reinterpret_cast<const uint32_t *>(qrow + ks * 16 + head0);
+          qf[ks][1] = *reinterpret_cast<const uint32_t *>(qrow + ks * 16 + head0 + 8);
+        } else {
+          qf[ks][0] = qf[ks][1] = 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          o[ks][i] = 0.f;
+      }
+      m0 = m1 = -INFINITY;
+      l0 = l1 = 0.f;
+    }
+
+    ok = __all_sync(0xffffffffu, mbar_wait(&bars[stage], (j / STAGES) & 1));
+    if (!ok)
+      break;
+
+    const uint32_t kbase = smem_u32(stages + stage * Shape::kStageBytes);
+    const uint32_t vbase = kbase + Shape::kTileBytes;
+    const uint32_t valid = min(uint32_t(kTileKeys), a.keys - (t % tpu) * kTileKeys);
+
+    // S^T = K Q^T for 16 keys x 8 heads; two accumulators for ILP.
+    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < KS; ks += 2) {
+      uint32_t fa[4];
+      ldmatrix_x4(fa, kbase + k_lane + ks * 32);
+      mma_f16_16816(sa, fa, qf[ks][0], qf[ks][1]);
+      if (ks + 1 < KS) {
+        uint32_t fb[4];
+        ldmatrix_x4(fb, kbase + k_lane + (ks + 1) * 32);
+        mma_f16_16816(sb, fb, qf[ks + 1][0], qf[ks + 1][1]);
+      }
+    }
+    float x0 = krow < valid ? (sa[0] + sb[0]) * a.scale_log2 : -INFINITY;
+    float x1 = krow < valid ? (sa[1] + sb[1]) * a.scale_log2 : -INFINITY;
+    float x2 = krow + 8 < valid ? (sa[2] + sb[2]) * a.scale_log2 : -INFINITY;
+    float x3 = krow + 8 < valid ? (sa[3] + sb[3]) * a.scale_log2 : -INFINITY;
+
+    float t0 = fmaxf(x0, x2), t1 = fmaxf(x1, x3);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
+      t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
+    }
+    const float n0 = fmaxf(m0, t0), n1 = fmaxf(m1, t1);
+    const float r0 = fast_exp2(m0 - n0), r1 = fast_exp2(m1 - n1);
+    m0 = n0;
+    m1 = n1;
+    const float p0 = fast_exp2(x0 - n0), p1 = fast_exp2(x1 - n1);
+    const float p2 = fast_exp2(x2 - n0), p3 = fast_exp2(x3 - n1);
+    l0 = l0 * r0 + p0 + p2;
+    l1 = l1 * r1 + p1 + p3;
+
+    const uint32_t b0 = movmatrix_trans(pack_half2(p0, p1));
+    const uint32_t b1 = movmatrix_trans(pack_half2(p2, p3));
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+      o[mt][0] *= r0;
+      o[mt][1] *= r1;
+      o[mt][2] *= r0;
+      o[mt][3] *= r1;
+      uint32_t fv[4];
+      ldmatrix_x4_trans(fv, vbase + v_lane + mt * 32);
+      mma_f16_16816(o[mt], fv, b0, b1);
+    }
+    __syncwarp();  // every lane is done with this stage before it is refilled
+    if (t + STAGES < end)
+      issue(t + STAGES, stage);
+  }
+
+  if (ok) {
+    flush(unit);
+    return;
+  }
+  // A wait gave up: let the copies already issued land (bounded) before the
+  // shared memory is released, and write nothing.
+  for (uint32_t r = t; r < min(end, t + STAGES); ++r) {
+    const uint32_t j = r - begin;
+    mbar_wait(&bars[j % STAGES], (j / STAGES) & 1);
+  }
+}
+
+// Partial pass for shapes outside the tensor-core kernel (any head_dim up to
+// 512, any group).  One CTA per (unit, key split); warps take query heads.
+__global__ void __launch_bounds__(128) partial_simt(const Args a) {
+  constexpr int kMaxPerLane = 16;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Partition pt = a.pt;
+  const uint32_t worker = blockIdx.x;  // tiles_per_worker == 1
+  const uint32_t unit = worker / pt.tiles_per_unit, split = worker % pt.tiles_per_unit;
+  if (unit >= pt.units)
+    return;
+  const uint32_t chunk = (a.keys + pt.tiles_per_unit - 1) / pt.tiles_per_unit;
+  const uint32_t k0 = split * chunk, k1 = min(a.keys, k0 + chunk);
+  const uint32_t seq = unit / a.kv_heads, kvh = unit % a.kv_heads;
+  const uint32_t D = a.head_dim, G = a.group;
+  float *rec = a.records + record_index(pt, worker, unit) * a.record_floats;
+  const __half *kbase = a.k + seq * a.cache_stride + size_t(kvh) * D;
+  const __half *vbase = a.v + seq * a.cache_stride + size_t(kvh) * D;
+  const size_t row = size_t(a.kv_heads) * D;
+
+  for (uint32_t h = warp; h < G; h += blockDim.x / 32) {
+    const __half *qrow = a.q + (size_t(seq) * a.kv_heads * G + kvh * G + h) * D;
+    float qv[kMaxPerLane], o[kMaxPerLane];
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      const uint32_t d = lane + 32 * i;
+      qv[i] = d < D ? __half2float(qrow[d]) : 0.f;
+      o[i] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    for (uint32_t key = k0; key < k1; ++key) {
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) {
+        const uint32_t d = lane + 32 * i;
+        if (d < D)
+          dot = fmaf(qv[i], __half2float(kbase[key * row + d]), dot);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+        dot += __shfl_xor_sync(0xffffffffu, dot, off);
+      const float x = dot * a.scale_log2;
+      const float n = fmaxf(m, x);
+      const float r = fast_exp2(m - n), p = fast_exp2(x - n);
+      l = l * r + p;
+      const __half ph = __float2half_rn(p);
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) {
+        const uint32_t d = lane + 32 * i;
+        if (d < D)
+          o[i] = fmaf(__half2float(ph), __half2float(vbase[key * row + d]), o[i] * r);
+      }
+      m = n;
+    }
+    if (lane == 0) {
+      rec[h] = m;
+      rec[G + h] = l;
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      const uint32_t d = lane + 32 * i;
+      if (d < D)
+        rec[2 * G + h * D + d] = o[i];
+    }
+  }
+}
+
+// Merge pass: one CTA per unit combines the records of every worker that
+// touched it and writes the group's fp16 outputs.
+__global__ void __launch_bounds__(256) merge(const Args a) {
+  const Partition pt = a.pt;
+  const uint32_t unit = blockIdx.x;
+  if (unit >= pt.units)
+    return;
+  const uint32_t seq = unit / a.kv_heads, kvh = unit % a.kv_heads;
+  const uint32_t G = a.group, D = a.head_dim;
+  const uint32_t w_lo = uint32_t((uint64_t(unit) * pt.tiles_per_unit) / pt.tiles_per_worker);
+  const uint32_t w_hi =
+      uint32_t((uint64_t(unit + 1) * pt.tiles_per_unit - 1) / pt.tiles_per_worker);
+  __half *out = a.out + (size_t(seq) * a.kv_heads * G + kvh * G) * D;
+  for (uint32_t i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const uint32_t h = i / D, d = i % D;
+    float top = -INFINITY;
+    for (uint32_t w = w_lo; w <= w_hi; ++w)
+      top = fmaxf(top, a.records[record_index(pt, w, unit) * a.record_floats + h]);
+    float sum = 0.f, acc = 0.f;
+    for (uint32_t w = w_lo; w <= w_hi; ++w) {
+      const float *rec = a.records + record_index(pt, w, unit) * a.record_floats;
+      const float e = fast_exp2(rec[h] - top);
+      sum = fmaf(rec[G + h], e, sum);
+      acc = fmaf(rec[2 * G + h * D + d], e, acc);
+    }
+    out[h * D + d] = __float2half_rn(acc / sum);
+  }
+}
+
+}  // namespace decode
+}  // namespace llmi

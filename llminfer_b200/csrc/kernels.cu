@@ -1,0 +1,379 @@
+// C ABI of the attention kernels (declared in include/llmi_cuda.h).
+//
+// All device code is compiled in this one translation unit so that the
+// device error word is a single symbol.  Each entry point validates its
+// arguments before launching anything, picks the kernel for the shape, and
+// reports launch errors through the status / last-error convention.
+#include "llmi_cuda.h"
+
+#include "cache_append.cuh"
+#include "common.cuh"
+#include "delta_recurrent.cuh"
+#include "gqa_decode.cuh"
+#include "gqa_flash_simt.cuh"
+#include "host/status.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <mutex>
+#include <utility>
+#include <vector>
+
+using namespace llmi;
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+cudaStream_t as_stream(void *stream) { return static_cast<cudaStream_t>(stream); }
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Opts a kernel in to more than 48 KiB of dynamic shared memory, once per
+// (kernel, device).
+int allow_smem(const void *kernel, size_t bytes, const DeviceInfo &dev) {
+  static std::mutex mutex;
+  static std::vector<std::pair<const void *, uint64_t>> done;  // kernel -> device bits
+  if (bytes > dev.max_smem_optin)
+    return fail(LLMI_UNSUPPORTED, "kernel needs %zu B of shared memory, device allows %zu", bytes,
+                dev.max_smem_optin);
+  std::lock_guard<std::mutex> lock(mutex);
+  const uint64_t bit = uint64_t(1) << dev.device;
+  for (auto &entry : done)
+    if (entry.first == kernel && (entry.second & bit))
+      return LLMI_OK;
+  if (int s = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              int(bytes)),
+                         "cudaFuncSetAttribute"))
+    return s;
+  for (auto &entry : done)
+    if (entry.first == kernel) {
+      entry.second |= bit;
+      return LLMI_OK;
+    }
+  done.emplace_back(kernel, bit);
+  return LLMI_OK;
+}
+
+int launched(const char *kernel) {
+  return check_cuda(cudaGetLastError(), kernel);
+}
+
+int check_gqa(const llmi_gqa_params *p, unsigned batch, const void *q, const void *k,
+              const void *v, size_t cache_stride, const void *out) {
+  if (!p || !q || !k || !v || !out)
+    return fail(LLMI_INVALID_ARGUMENT, "GQA: null parameter or tensor pointer");
+  if (!batch || !p->tokens || !p->queryHeads || !p->kvHeads || !p->headDim)
+    return fail(LLMI_INVALID_ARGUMENT, "GQA: batch, tokens, heads and head_dim must be positive");
+  if (p->queryHeads % p->kvHeads)
+    return fail(LLMI_INVALID_ARGUMENT, "GQA: %u query heads are not a multiple of %u kv heads",
+                p->queryHeads, p->kvHeads);
+  const uint64_t rows = uint64_t(p->past) + p->tokens;
+  if (rows > UINT32_MAX)
+    return fail(LLMI_INVALID_ARGUMENT, "GQA: past + tokens exceeds 32 bits");
+  if (batch > 1 && cache_stride < rows * p->kvHeads * p->headDim)
+    return fail(LLMI_INVALID_ARGUMENT,
+                "GQA: cache stride %zu cannot hold %llu rows of %u x %u", cache_stride,
+                (unsigned long long)rows, p->kvHeads, p->headDim);
+  return LLMI_OK;
+}
+
+// ---- decode planning -------------------------------------------------------
+
+struct DecodePlan {
+  enum Kind { Mma256, Mma128, Mma64, Simt } kind = Simt;
+  decode::Partition pt{};
+  uint32_t record_floats = 0;
+  uint32_t grid = 0, threads = 0;
+  size_t smem = 0;
+  size_t workspace = 0;
+};
+
+constexpr int kWarps256 = 4, kStages256 = 3;
+constexpr int kWarps128 = 8, kStages128 = 3;
+constexpr int kWarps64 = 8, kStages64 = 4;
+
+// Picks the decode kernels and the work partition.  The tensor-core partial
+// pass needs 16-byte aligned operands (bulk copies) and a supported shape;
+// everything else takes the CUDA-core pass.
+int plan_decode(const llmi_gqa_params &p, unsigned batch, bool aligned, const DeviceInfo &dev,
+                DecodePlan &plan) {
+  const uint32_t D = p.headDim, G = p.queryHeads / p.kvHeads;
+  const uint32_t keys = p.past + 1;
+  const uint32_t units = batch * p.kvHeads;
+  plan.record_floats = decode::record_floats(G, D);
+  const bool fits = G <= 8 && (D == 256 || D == 128 || D == 64);
+  if (fits && aligned) {
+    int warps, smem;
+    if (D == 256) {
+      plan.kind = DecodePlan::Mma256;
+      warps = kWarps256;
+      smem = decode::MmaShape<256, kWarps256, kStages256>::kSmemBytes;
+    } else if (D == 128) {
+      plan.kind = DecodePlan::Mma128;
+      warps = kWarps128;
+      smem = decode::MmaShape<128, kWarps128, kStages128>::kSmemBytes;
+    } else {
+      plan.kind = DecodePlan::Mma64;
+      warps = kWarps64;
+      smem = decode::MmaShape<64, kWarps64, kStages64>::kSmemBytes;
+    }
+    const uint32_t tpu = (keys + decode::kTileKeys - 1) / decode::kTileKeys;
+    const uint64_t tiles = uint64_t(units) * tpu;
+    if (tiles > UINT32_MAX)
+      return fail(LLMI_UNSUPPORTED, "decode: %llu key tiles exceed 32 bits",
+                  (unsigned long long)tiles);
+    const uint64_t workers_max = uint64_t(dev.sm_count) * warps;
+    const uint32_t tpw = uint32_t((tiles + workers_max - 1) / workers_max);
+    const uint32_t busy = uint32_t((tiles + tpw - 1) / tpw);
+    plan.grid = (busy + warps - 1) / warps;
+    plan.threads = warps * 32;
+    plan.smem = size_t(smem);
+    plan.pt.units = units;
+    plan.pt.tiles_per_unit = tpu;
+    plan.pt.tiles_per_worker = tpw;
+    plan.pt.max_span = std::min<uint32_t>(units, (tpw + tpu - 1) / tpu + 1);
+    plan.pt.workers = plan.grid * warps;
+  } else {
+    if (D > 512)
+      return fail(LLMI_UNSUPPORTED, "decode: head_dim %u above 512", D);
+    plan.kind = DecodePlan::Simt;
+    const uint32_t want = (4u * dev.sm_count + units - 1) / units;
+    const uint32_t splits = std::max(1u, std::min(keys, want));
+    plan.pt.units = units;
+    plan.pt.tiles_per_unit = splits;
+    plan.pt.tiles_per_worker = 1;
+    plan.pt.max_span = 1;
+    plan.pt.workers = units * splits;
+    plan.grid = plan.pt.workers;
+    plan.threads = 128;
+    plan.smem = 0;
+  }
+  plan.workspace = size_t(plan.pt.workers) * plan.pt.max_span * plan.record_floats * sizeof(float);
+  return LLMI_OK;
+}
+
+template <int D, int WARPS, int STAGES>
+int launch_decode_mma(const DecodePlan &plan, const decode::Args &args, const DeviceInfo &dev,
+                      cudaStream_t stream) {
+  auto kernel = decode::partial_mma<D, WARPS, STAGES>;
+  if (int s = allow_smem(reinterpret_cast<const void *>(kernel), plan.smem, dev))
+    return s;
+  kernel<<<plan.grid, plan.threads, plan.smem, stream>>>(args);
+  return launched("gqaScores (decode partial, tensor cores)");
+}
+
+}  // namespace
+
+// ---- cacheAppend -------------------------------------------------------------
+
+extern "C" int llmi_cuda_cache_append(const llmi_cache_params *p, unsigned batch,
+                                      const uint16_t *input, size_t input_stride,
+                                      uint16_t *cache, size_t cache_stride, void *stream) {
+  clear_error();
+  if (!p || !input || !cache || !batch)
+    return fail(LLMI_INVALID_ARGUMENT, "cacheAppend: null pointer or zero batch");
+  if (p->count == 0)
+    return LLMI_OK;
+  if (batch > 1 && (input_stride < p->count || cache_stride < uint64_t(p->offset) + p->count))
+    return fail(LLMI_INVALID_ARGUMENT, "cacheAppend: sequence strides overlap");
+  AppendArgs a{input, cache, input_stride, cache_stride, p->count, p->offset, batch};
+  const bool vec = p->count % 8 == 0 && p->offset % 8 == 0 && aligned16(input) &&
+                   aligned16(cache) && (batch == 1 || (input_stride % 8 == 0 && cache_stride % 8 == 0));
+  const uint64_t work = vec ? uint64_t(p->count / 8) * batch : uint64_t(p->count) * batch;
+  const uint32_t grid = uint32_t(std::min<uint64_t>((work + 255) / 256, 4096));
+  if (vec)
+    cache_append_v8<<<grid, 256, 0, as_stream(stream)>>>(a);
+  else
+    cache_append_scalar<<<grid, 256, 0, as_stream(stream)>>>(a);
+  return launched("cacheAppend");
+}
+
+// ---- gqaFlashAttention ------------------------------------------------------------
+
+extern "C" int llmi_cuda_gqa_prefill(const llmi_gqa_params *p, unsigned batch,
+                                     const uint16_t *q, const uint16_t *k_cache,
+                                     const uint16_t *v_cache, size_t cache_stride,
+                                     uint16_t *out, void *stream) {
+  clear_error();
+  if (int s = check_gqa(p, batch, q, k_cache, v_cache, cache_stride, out))
+    return s;
+  DeviceInfo dev;
+  if (int s = current_device(dev))
+    return s;
+  if (p->headDim > flash_simt::kMaxPerLane * 32)
+    return fail(LLMI_UNSUPPORTED, "gqaFlashAttention: head_dim %u above 256", p->headDim);
+  if (batch > 65535 || p->queryHeads > 65535)
+    return fail(LLMI_UNSUPPORTED, "gqaFlashAttention: batch or heads above 65535");
+  flash_simt::Args a;
+  a.q = reinterpret_cast<const __half *>(q);
+  a.k = reinterpret_cast<const __half *>(k_cache);
+  a.v = reinterpret_cast<const __half *>(v_cache);
+  a.cache_stride = cache_stride;
+  a.out = reinterpret_cast<__half *>(out);
+  a.tokens = p->tokens;
+  a.q_heads = p->queryHeads;
+  a.kv_heads = p->kvHeads;
+  a.head_dim = p->headDim;
+  a.past = p->past;
+  a.group = p->queryHeads / p->kvHeads;
+  a.scale_log2 = kLog2e / std::sqrt(float(p->headDim));
+  const size_t smem = flash_simt::smem_bytes(p->headDim);
+  if (int s = allow_smem(reinterpret_cast<const void *>(flash_simt::attend), smem, dev))
+    return s;
+  dim3 grid((p->tokens + flash_simt::kWarps - 1) / flash_simt::kWarps, p->queryHeads, batch);
+  flash_simt::attend<<<grid, flash_simt::kWarps * 32, smem, as_stream(stream)>>>(a);
+  return launched("gqaFlashAttention (CUDA cores)");
+}
+
+// ---- decode: gqaScores + gqaSoftmax ---------------------------------------------------
+
+extern "C" size_t llmi_cuda_gqa_decode_workspace(const llmi_gqa_params *p, unsigned batch) {
+  clear_error();
+  if (!p || !batch || !p->queryHeads || !p->kvHeads || !p->headDim ||
+      p->queryHeads % p->kvHeads) {
+    fail(LLMI_INVALID_ARGUMENT, "decode workspace: invalid shape");
+    return 0;
+  }
+  DeviceInfo dev;
+  if (current_device(dev))
+    return 0;
+  // Operand alignment is not known yet: size for whichever pass runs.
+  DecodePlan fast, simt;
+  const int a = plan_decode(*p, batch, true, dev, fast);
+  const int b = plan_decode(*p, batch, false, dev, simt);
+  if (a && b)
+    return 0;
+  clear_error();
+  return std::max(a ? 0 : fast.workspace, b ? 0 : simt.workspace);
+}
+
+extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, const uint16_t *q,
+                                    const uint16_t *k_cache, const uint16_t *v_cache,
+                                    size_t cache_stride, uint16_t *out, void *workspace,
+                                    size_t workspace_bytes, void *stream) {
+  clear_error();
+  if (int s = check_gqa(p, batch, q, k_cache, v_cache, cache_stride, out))
+    return s;
+  if (p->tokens != 1)
+    return fail(LLMI_UNSUPPORTED, "decode: %u tokens; the decode path takes one token (use prefill)",
+                p->tokens);
+  if (!workspace)
+    return fail(LLMI_INVALID_ARGUMENT, "decode: null workspace");
+  DeviceInfo dev;
+  if (int s = current_device(dev))
+    return s;
+  DecodePlan plan;
+  const bool aligned = aligned16(q) && aligned16(k_cache) && aligned16(v_cache) &&
+                       (batch == 1 || cache_stride % 8 == 0);
+  if (int s = plan_decode(*p, batch, aligned, dev, plan))
+    return s;
+  if (workspace_bytes < plan.workspace)
+    return fail(LLMI_WORKSPACE_TOO_SMALL, "decode: workspace of %zu B, %zu B needed",
+                workspace_bytes, plan.workspace);
+  if (!aligned16(workspace))
+    return fail(LLMI_INVALID_ARGUMENT, "decode: workspace must be 16-byte aligned");
+
+  decode::Args a;
+  a.q = reinterpret_cast<const __half *>(q);
+  a.k = reinterpret_cast<const __half *>(k_cache);
+  a.v = reinterpret_cast<const __half *>(v_cache);
+  a.cache_stride = cache_stride;
+  a.out = reinterpret_cast<__half *>(out);
+  a.records = static_cast<float *>(workspace);
+  a.pt = plan.pt;
+  a.kv_heads = p->kvHeads;
+  a.group = p->queryHeads / p->kvHeads;
+  a.head_dim = p->headDim;
+  a.keys = p->past + 1;
+  a.record_floats = plan.record_floats;
+  a.scale_log2 = kLog2e / std::sqrt(float(p->headDim));
+  cudaStream_t s = as_stream(stream);
+  int status = LLMI_OK;
+  switch (plan.kind) {
+  case DecodePlan::Mma256:
+    status = launch_decode_mma<256, kWarps256, kStages256>(plan, a, dev, s);
+    break;
+  case DecodePlan::Mma128:
+    status = launch_decode_mma<128, kWarps128, kStages128>(plan, a, dev, s);
+    break;
+  case DecodePlan::Mma64:
+    status = launch_decode_mma<64, kWarps64, kStages64>(plan, a, dev, s);
+    break;
+  case DecodePlan::Simt:
+    decode::partial_simt<<<plan.grid, plan.threads, 0, s>>>(a);
+    status = launched("gqaScores (decode partial, CUDA cores)");
+    break;
+  }
+  if (status)
+    return status;
+  decode::merge<<<plan.pt.units, 256, 0, s>>>(a);
+  return launched("gqaSoftmax (decode merge)");
+}
+
+// ---- graphDeltaUpdate ----------------------------------------------------------------
+
+extern "C" int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch, const float *q,
+                                      const float *k, const uint16_t *v, const float *beta,
+                                      const float *decay, float *state, uint16_t *out,
+                                      void *stream) {
+  clear_error();
+  if (!p || !q || !k || !v || !beta || !decay || !state || !out)
+    return fail(LLMI_INVALID_ARGUMENT, "DeltaUpdate: null parameter or tensor pointer");
+  if (!batch || !p->tokens || !p->keyHeads || !p->keyDim || !p->valueHeads || !p->valueDim)
+    return fail(LLMI_INVALID_ARGUMENT, "DeltaUpdate: sizes must be positive");
+  if (p->valueHeads % p->keyHeads)
+    return fail(LLMI_INVALID_ARGUMENT, "DeltaUpdate: %u value heads are not a multiple of %u",
+                p->valueHeads, p->keyHeads);
+  delta::Args a;
+  a.q = q;
+  a.k = k;
+  a.v = reinterpret_cast<const __half *>(v);
+  a.beta = beta;
+  a.decay = decay;
+  a.state = state;
+  a.out = reinterpret_cast<__half *>(out);
+  a.batch = batch;
+  a.tokens = p->tokens;
+  a.key_heads = p->keyHeads;
+  a.key_dim = p->keyDim;
+  a.value_heads = p->valueHeads;
+  a.value_dim = p->valueDim;
+  a.group = p->valueHeads / p->keyHeads;
+  cudaStream_t s = as_stream(stream);
+  const bool fast = p->valueDim == 128 && (p->keyDim == 128 || p->keyDim == 64) &&
+                    aligned16(state) && aligned16(v) && batch <= 65535 &&
+                    p->valueHeads <= 2147483647u;
+  if (fast) {
+    dim3 grid(p->valueHeads, batch);
+    if (p->keyDim == 128)
+      delta::recurrent_v128<128><<<grid, delta::kRecWarps * 32, 0, s>>>(a);
+    else
+      delta::recurrent_v128<64><<<grid, delta::kRecWarps * 32, 0, s>>>(a);
+    return launched("graphDeltaUpdate (recurrent, registers)");
+  }
+  const uint64_t columns = uint64_t(batch) * p->valueHeads * p->valueDim;
+  delta::recurrent_generic<<<uint32_t((columns + 127) / 128), 128, 0, s>>>(a);
+  return launched("graphDeltaUpdate (recurrent, generic)");
+}
+
+// ---- device error word ---------------------------------------------------------------
+
+extern "C" int llmi_cuda_poll_error(void *stream) {
+  clear_error();
+  if (int s = check_cuda(cudaStreamSynchronize(as_stream(stream)), "stream synchronize"))
+    return s;
+  unsigned word = 0;
+  if (int s = check_cuda(cudaMemcpyFromSymbol(&word, g_error_word, sizeof word), "read error word"))
+    return s;
+  if (!word)
+    return LLMI_OK;
+  const unsigned zero = 0;
+  if (int s = check_cuda(cudaMemcpyToSymbol(g_error_word, &zero, sizeof zero), "clear error word"))
+    return s;
+  return fail(LLMI_DEVICE_TIMEOUT, "device error word 0x%x:%s%s%s", word,
+              (word & kErrWaitTimeout) ? " wait-timeout" : "",
+              (word & kErrTmemAlloc) ? " tmem-alloc" : "",
+              (word & kErrBadLaunch) ? " bad-launch" : "");
+}

@@ -1,0 +1,225 @@
+"""torch-facing wrappers of the C ABI (include/llmi_cuda.h).
+
+PyTorch only provides device memory and streams here; every op runs the CUDA
+kernels of libllmi_cuda.so.  Shapes follow the reference's operands with a
+leading sequence (batch) dimension:
+
+  GQA       q, out        [B, T, Hq, D]       fp16
+            k/v cache     [B, capacity, Hkv, D] fp16
+  DeltaNet  q, k          [B, T, Hk*dk]       fp32
+            v, out        [B, T, Hv*dv]       fp16
+            beta, decay   [B, T, Hv]          fp32
+            state         [B, Hv, dk, dv]     fp32 (updated in place)
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _abi as abi
+from ._abi import LlmiError, check, lib
+
+
+def _stream(stream: torch.cuda.Stream | None) -> int:
+    s = torch.cuda.current_stream() if stream is None else stream
+    return s.cuda_stream
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous CUDA {dtype} tensor "
+                         f"(got {t.dtype} on {t.device}, contiguous={t.is_contiguous()})")
+
+
+def cache_append(rows: torch.Tensor, cache: torch.Tensor, past: int,
+                 stream: torch.cuda.Stream | None = None) -> None:
+    """cacheAppend: writes rows [B, T, Hkv, D] into cache [B, cap, Hkv, D] at [past, past+T)."""
+    _need(rows, torch.float16, "rows")
+    _need(cache, torch.float16, "cache")
+    B, T, H, D = rows.shape
+    if cache.shape[0] != B or cache.shape[2:] != (H, D) or past + T > cache.shape[1]:
+        raise ValueError("cache_append: rows do not fit the cache")
+    row = H * D
+    p = abi.CacheParams(T * row, past * row)
+    check(lib.llmi_cuda_cache_append(ctypes.byref(p), B, rows.data_ptr(), T * row,
+                                     cache.data_ptr(), cache.shape[1] * row, _stream(stream)))
+
+
+def _gqa_params(q, k_cache, past):
+    B, T, Hq, D = q.shape
+    if k_cache.shape[0] != B or k_cache.shape[3] != D:
+        raise ValueError("q and cache shapes disagree")
+    return abi.GqaParams(T, Hq, k_cache.shape[2], D, past)
+
+
+def gqa_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, past: int,
+                out: torch.Tensor | None = None,
+                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """gqaFlashAttention over cache rows [0, past+T) (T >= 1)."""
+    for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _need(t, torch.float16, n)
+    p = _gqa_params(q, k_cache, past)
+    out = torch.empty_like(q) if out is None else out
+    _need(out, torch.float16, "out")
+    stride = k_cache[0].numel()
+    check(lib.llmi_cuda_gqa_prefill(ctypes.byref(p), q.shape[0], q.data_ptr(),
+                                    k_cache.data_ptr(), v_cache.data_ptr(), stride,
+                                    out.data_ptr(), _stream(stream)))
+    return out
+
+
+def decode_workspace_bytes(batch: int, query_heads: int, kv_heads: int, head_dim: int,
+                           past: int) -> int:
+    p = abi.GqaParams(1, query_heads, kv_heads, head_dim, past)
+    n = lib.llmi_cuda_gqa_decode_workspace(ctypes.byref(p), batch)
+    if n == 0:
+        raise LlmiError(abi.LLMI_CUDA_ERROR, lib.llmi_cuda_last_error().decode())
+    return n
+
+
+def gqa_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, past: int,
+               out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+               stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """gqaScores + gqaSoftmax: one query token per sequence over cache rows [0, past+1)."""
+    for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _need(t, torch.float16, n)
+    p = _gqa_params(q, k_cache, past)
+    if workspace is None:
+        n = decode_workspace_bytes(q.shape[0], p.queryHeads, p.kvHeads, p.headDim, past)
+        workspace = torch.empty(n, dtype=torch.uint8, device=q.device)
+    out = torch.empty_like(q) if out is None else out
+    _need(out, torch.float16, "out")
+    stride = k_cache[0].numel()
+    check(lib.llmi_cuda_gqa_decode(ctypes.byref(p), q.shape[0], q.data_ptr(),
+                                   k_cache.data_ptr(), v_cache.data_ptr(), stride,
+                                   out.data_ptr(), workspace.data_ptr(), workspace.numel(),
+                                   _stream(stream)))
+    return out
+
+
+def delta_update(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
+                 decay: torch.Tensor, state: torch.Tensor, out: torch.Tensor | None = None,
+                 stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """graphDeltaUpdate: updates state [B, Hv, dk, dv] in place, returns out [B, T, Hv*dv]."""
+    for t, n in ((q, "q"), (k, "k"), (beta, "beta"), (decay, "decay"), (state, "state")):
+        _need(t, torch.float32, n)
+    _need(v, torch.float16, "v")
+    B, T, key_width = q.shape
+    _, Hv, dk, dv = state.shape
+    p = abi.DeltaParams(T, key_width // dk, dk, Hv, dv)
+    out = torch.empty_like(v) if out is None else out
+    _need(out, torch.float16, "out")
+    check(lib.llmi_cuda_delta_update(ctypes.byref(p), B, q.data_ptr(), k.data_ptr(),
+                                     v.data_ptr(), beta.data_ptr(), decay.data_ptr(),
+                                     state.data_ptr(), out.data_ptr(), _stream(stream)))
+    return out
+
+
+def poll_error(stream: torch.cuda.Stream | None = None) -> None:
+    check(lib.llmi_cuda_poll_error(_stream(stream)))
+
+
+@dataclass
+class LayerTensors:
+    """One layer's step operands (see LayerIO in llmi_cuda.h)."""
+    q: torch.Tensor
+    k: torch.Tensor
+    v: torch.Tensor
+    out: torch.Tensor
+    beta: torch.Tensor | None = None
+    decay: torch.Tensor | None = None
+
+    def to_abi(self) -> abi.LayerIO:
+        ptr = lambda t: None if t is None else t.data_ptr()
+        return abi.LayerIO(ptr(self.q), ptr(self.k), ptr(self.v), ptr(self.beta),
+                           ptr(self.decay), ptr(self.out))
+
+
+class AttentionSession:
+    """The attention-stack session (llmi_cuda_session_*), a MetalSession for the attention ops."""
+
+    def __init__(self, kinds, batch, capacity, query_heads=0, kv_heads=0, head_dim=0,
+                 key_heads=0, key_dim=0, value_heads=0, value_dim=0,
+                 stream: torch.cuda.Stream | None = None):
+        self.kinds = list(kinds)
+        self.batch, self.capacity = batch, capacity
+        self.shape = dict(query_heads=query_heads, kv_heads=kv_heads, head_dim=head_dim,
+                          key_heads=key_heads, key_dim=key_dim, value_heads=value_heads,
+                          value_dim=value_dim)
+        self.stream = torch.cuda.Stream() if stream is None else stream
+        self._cfg, self._kinds = abi.make_stack_config(self.kinds, batch, capacity, query_heads,
+                                                       kv_heads, head_dim, key_heads, key_dim,
+                                                       value_heads, value_dim)
+        handle = ctypes.c_void_p()
+        check(lib.llmi_cuda_session_open(ctypes.byref(self._cfg), self.stream.cuda_stream,
+                                         ctypes.byref(handle)))
+        self._handle = handle
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None):
+            lib.llmi_cuda_session_close(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        self.close()
+
+    def _io(self, layers):
+        if len(layers) != len(self.kinds):
+            raise ValueError(f"{len(layers)} layer operand sets for {len(self.kinds)} layers")
+        return (abi.LayerIO * len(layers))(*[x.to_abi() for x in layers])
+
+    def step(self, tokens: int, layers, trace_plan: bool = False) -> None:
+        self._sync_inputs()
+        check(lib.llmi_cuda_session_step(self._handle, tokens, self._io(layers), int(trace_plan)))
+
+    def enqueue(self, tokens: int, layers) -> None:
+        check(lib.llmi_cuda_session_enqueue(self._handle, tokens, self._io(layers)))
+
+    def sync(self) -> None:
+        check(lib.llmi_cuda_session_sync(self._handle))
+
+    def reset(self) -> None:
+        check(lib.llmi_cuda_session_reset(self._handle))
+
+    def _sync_inputs(self) -> None:
+        # Operands produced on torch's current stream must be ready before the
+        # session stream reads them.
+        self.stream.wait_stream(torch.cuda.current_stream())
+
+    @property
+    def past(self) -> int:
+        return lib.llmi_cuda_session_past(self._handle)
+
+    @property
+    def invalid(self) -> bool:
+        return bool(lib.llmi_cuda_session_is_invalid(self._handle))
+
+    def plan(self) -> list[dict]:
+        import json
+        n = lib.llmi_cuda_session_plan(self._handle, None, 0)
+        buf = ctypes.create_string_buffer(n + 1)
+        lib.llmi_cuda_session_plan(self._handle, buf, n + 1)
+        return [json.loads(line) for line in buf.value.decode().splitlines() if line]
+
+    def _state_shape(self, which: int):
+        s = self.shape
+        if which == abi.STATE_RECURRENT:
+            return (self.batch, s["value_heads"], s["key_dim"], s["value_dim"]), torch.float32
+        return (self.batch, self.capacity, s["kv_heads"], s["head_dim"]), torch.float16
+
+    def read_state(self, layer: int, which: int) -> torch.Tensor:
+        shape, dtype = self._state_shape(which)
+        t = torch.empty(shape, dtype=dtype, device="cuda")
+        torch.cuda.current_stream().synchronize()
+        check(lib.llmi_cuda_session_read_state(self._handle, layer, which, t.data_ptr(),
+                                               t.numel() * t.element_size()))
+        return t
+
+    def write_state(self, layer: int, which: int, value: torch.Tensor) -> None:
+        shape, dtype = self._state_shape(which)
+        value = value.to(device="cuda", dtype=dtype).contiguous().reshape(shape)
+        torch.cuda.current_stream().synchronize()
+        check(lib.llmi_cuda_session_write_state(self._handle, layer, which, value.data_ptr(),
+                                                value.numel() * value.element_size()))

@@ -1,0 +1,128 @@
+"""GQA parity on the GPU: cacheAppend, prefill (gqaFlashAttention) and
+decode (gqaScores + gqaSoftmax), through the C ABI, against the CPU oracle.
+
+Bars: the reference's own known-answer tolerance |a - e| <= 2e-4 + 5e-4|e|
+(tests/FlashAttentionTest.mm:80-81) on its two KAT cases, and the acceptance
+bar max-abs <= 1e-2, rel-L2 <= 2e-3 against the fp64 dense oracle elsewhere.
+Outputs are pre-filled with NaN (as FlashAttentionTest.mm:41 does) so an
+unwritten element fails.
+"""
+import numpy as np
+import pytest
+import torch
+
+import _inputs
+import _oracle
+from llminfer_b200 import abi, ops
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = _oracle.ROOT / "tests" / "golden"
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def nan_like(t):
+    return torch.full_like(t, float("nan"))
+
+
+def check_bar(got, expected):
+    got = got.float().cpu().numpy() if isinstance(got, torch.Tensor) else got
+    assert np.isfinite(got).all(), "unwritten or non-finite outputs"
+    max_abs, rel = _inputs.errors(got, expected)
+    assert max_abs <= _inputs.MAX_ABS and rel <= _inputs.REL_L2, (max_abs, rel)
+    return max_abs, rel
+
+
+@pytest.mark.parametrize("case", [0, 1])
+def test_prefill_known_answers(case):
+    kat = np.load(GOLDEN / "gqa_kat.npz")
+    T, Hq, Hkv, D, past = (int(x) for x in kat[f"case{case}_shape"])
+    q = dev(kat[f"case{case}_q"].view(np.float16).reshape(1, T, Hq, D))
+    k = dev(kat[f"case{case}_k"].view(np.float16).reshape(1, past + T, Hkv, D))
+    v = dev(kat[f"case{case}_v"].view(np.float16).reshape(1, past + T, Hkv, D))
+    out = ops.gqa_prefill(q, k, v, past, out=nan_like(q))
+    torch.cuda.synchronize()
+    got = out.double().cpu().numpy()
+    expected = kat[f"case{case}_expected"].reshape(1, T, Hq, D)
+    assert np.all(np.abs(got - expected) <= 2e-4 + 5e-4 * np.abs(expected))
+
+
+@pytest.mark.parametrize("batch,tokens,past,hq,hkv,d", [
+    (1, 128, 0, 16, 4, 256),   # the prefill benchmark config (C1)
+    (2, 33, 17, 8, 2, 64),
+    (2, 5, 0, 4, 4, 128),
+    (3, 70, 130, 16, 4, 256),
+    (2, 19, 3, 4, 2, 12),      # odd head_dim (CUDA-core path)
+    (1, 9, 40, 6, 2, 40),
+])
+def test_prefill_matches_dense_oracle(batch, tokens, past, hq, hkv, d):
+    q, k, v = _inputs.gqa_case(batch, tokens, past, hq, hkv, d, capacity=past + tokens + 3,
+                               seed=100 + tokens)
+    out = ops.gqa_prefill(dev(q), dev(k), dev(v), past, out=nan_like(dev(q)))
+    check_bar(out, _oracle.gqa_dense(q, k, v, past))
+
+
+@pytest.mark.parametrize("batch,past,hq,hkv,d", [
+    (3, 0, 16, 4, 256),
+    (3, 15, 16, 4, 256),
+    (2, 16, 16, 4, 256),
+    (2, 1000, 16, 4, 256),
+    (2, 77, 8, 8, 128),
+    (2, 300, 16, 2, 256),      # group of 8 query heads
+    (2, 33, 8, 1, 64),
+    (2, 50, 4, 2, 12),         # odd head_dim (CUDA-core path)
+    (2, 20, 24, 2, 64),        # group of 12 (CUDA-core path)
+])
+def test_decode_matches_oracles(batch, past, hq, hkv, d):
+    q, k, v = _inputs.gqa_case(batch, 1, past, hq, hkv, d, capacity=past + 5, seed=7 + past)
+    out = ops.gqa_decode(dev(q), dev(k), dev(v), past, out=nan_like(dev(q)))
+    got = out.float().cpu().numpy()
+    check_bar(got, _oracle.gqa_dense(q, k, v, past))
+    # The reference decode path (fp16 scores and probabilities) agrees too.
+    max_abs, rel = _inputs.errors(got, _oracle.gqa_eager_f16(q, k, v, past))
+    assert max_abs <= _inputs.MAX_ABS and rel <= 5e-3, (max_abs, rel)
+
+
+def test_decode_benchmark_shape_reduced_batch():
+    # C2 per-sequence shape: past 4096 in a capacity-8192 cache.
+    q, k, v = _inputs.gqa_case(6, 1, 4096, 16, 4, 256, capacity=8192, seed=11)
+    out = ops.gqa_decode(dev(q), dev(k), dev(v), 4096, out=nan_like(dev(q)))
+    check_bar(out, _oracle.gqa_dense(q, k, v, 4096))
+
+
+def test_decode_and_prefill_agree_on_one_token():
+    q, k, v = _inputs.gqa_case(4, 1, 513, 16, 4, 256, seed=12)
+    a = ops.gqa_decode(dev(q), dev(k), dev(v), 513)
+    b = ops.gqa_prefill(dev(q), dev(k), dev(v), 513)
+    max_abs, rel = _inputs.errors(a.float().cpu().numpy(), b.float().cpu().numpy())
+    assert max_abs <= 4e-3 and rel <= 2e-3
+
+
+def test_decode_rejects_small_workspace():
+    q, k, v = _inputs.gqa_case(2, 1, 100, 16, 4, 256, seed=13)
+    need = ops.decode_workspace_bytes(2, 16, 4, 256, 100)
+    small = torch.empty(need - 16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(abi.LlmiError) as err:
+        ops.gqa_decode(dev(q), dev(k), dev(v), 100, workspace=small)
+    assert err.value.status == abi.LLMI_WORKSPACE_TOO_SMALL
+
+
+@pytest.mark.parametrize("tokens,past,hkv,d", [(1, 4096, 4, 256), (17, 5, 2, 64), (3, 0, 1, 12)])
+def test_cache_append_is_exact(tokens, past, hkv, d):
+    batch, cap = 3, past + tokens + 2
+    cache = _inputs.half_normal(1, 50, (batch, cap, hkv, d))
+    rows = _inputs.half_normal(1, 51, (batch, tokens, hkv, d))
+    got = dev(cache)
+    ops.cache_append(dev(rows), got, past)
+    expected = cache.copy()
+    expected[:, past:past + tokens] = rows
+    np.testing.assert_array_equal(got.cpu().numpy().view(np.uint16), expected.view(np.uint16))
+
+
+def test_poll_error_is_clean_after_work():
+    q, k, v = _inputs.gqa_case(2, 1, 64, 16, 4, 256, seed=14)
+    ops.gqa_decode(dev(q), dev(k), dev(v), 64)
+    ops.poll_error()
