@@ -85,56 +85,76 @@ def profile_traffic(name: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    """SM clocks and clock-event (throttle) reasons sampled every 100 ms during the timed
+    region, read through NVML (read-only queries)."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {  # NVML clocks-event reason bits
+        0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+        0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown",
+    }
 
-    def __init__(self, device_id: str):
-        self.index = device_id  # nvidia-smi --id: index or GPU UUID
-        self.proc = None
-        self.file = None
+    def __init__(self, torch, device):
+        import threading
+        self.samples = []
+        self.max_mhz = None
+        self.error = None
+        self.stop = threading.Event()
+        self.thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            want = str(torch.cuda.get_device_properties(device).uuid).lower()
+            self.handle = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                uuid = pynvml.nvmlDeviceGetUUID(h)
+                uuid = uuid.decode() if isinstance(uuid, bytes) else uuid
+                if want and want in uuid.lower():
+                    self.handle = h
+            if self.handle is None:
+                raise RuntimeError(f"no NVML device with uuid {want}")
+            self.nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._run, daemon=True)
+        except Exception as exc:  # NVML missing or no match: report, do not fail the bench
+            self.error = f"clock sampling unavailable: {exc}"
+
+    def _reasons(self):
+        n = self.nvml
+        for name in ("nvmlDeviceGetCurrentClocksEventReasons",
+                     "nvmlDeviceGetCurrentClocksThrottleReasons"):
+            if hasattr(n, name):
+                return getattr(n, name)(self.handle)
+        return 0
+
+    def _run(self):
+        while not self.stop.is_set():
+            try:
+                sm = self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+                self.samples.append((sm, self._reasons()))
+            except Exception as exc:
+                self.error = str(exc)
+                return
+            self.stop.wait(0.1)
 
     def __enter__(self):
-        try:
-            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=self.file, stderr=subprocess.DEVNULL)
-        except (OSError, ValueError):
-            self.proc = None
+        if self.thread is not None:
+            self.thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self.stop.set()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
 
     def summary(self):
-        if self.proc is None or self.file is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.file.flush()
-        rows = []
-        with open(self.file.name) as f:
-            for line in f:
-                parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
-        os.unlink(self.file.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz,
+                    "reasons": [self.error or "no samples"]}
+        reasons = sorted({name for _, bits in self.samples
+                          for bit, name in self.REASONS.items() if bits & bit})
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples)}
 
 
 class Dist:
@@ -285,11 +305,7 @@ def run_ours(args, dist):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(K)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    try:
-        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
-    except (AttributeError, RuntimeError):
-        gpu_id = str(device.index)
-    with ClockSampler(gpu_id) as clocks:
+    with ClockSampler(torch, device) as clocks:
         start.record()
         for i in range(K):
             ops.cache_append(kn, kc, P)

@@ -38,12 +38,21 @@ constexpr int kTileKeys = 16;
 // How the key tiles of all units are divided among workers.  Worker w owns
 // tiles [w*tiles_per_worker, (w+1)*tiles_per_worker) of the concatenation of
 // the units' tile lists and writes one record per unit it touches.
+//
+// Two shapes of worker:
+//  * heads == 1: a worker is one warp and a unit is one (sequence, kv head);
+//  * heads == Hkv: a worker is one CTA whose warp h serves kv head h, and a
+//    unit is one sequence.  The CTA's warps then stream the same key rows of
+//    every kv head together, so each 2 KiB cache row [Hkv][D] is fetched as a
+//    whole by one SM at one time.
+// Records are laid out [worker][span][heads].
 struct Partition {
-  uint32_t units;             // batch * kvHeads
+  uint32_t units;             // sequences * (kv heads when heads == 1)
   uint32_t tiles_per_unit;    // key tiles (or key splits) per unit
   uint32_t tiles_per_worker;
-  uint32_t max_span;          // records reserved per worker
+  uint32_t max_span;          // units a worker can touch
   uint32_t workers;
+  uint32_t heads;             // kv heads served by one worker
 };
 
 __host__ __device__ inline uint32_t first_unit(const Partition &pt, uint32_t worker) {
@@ -51,8 +60,17 @@ __host__ __device__ inline uint32_t first_unit(const Partition &pt, uint32_t wor
 }
 
 __host__ __device__ inline uint64_t record_index(const Partition &pt, uint32_t worker,
-                                                 uint32_t unit) {
-  return uint64_t(worker) * pt.max_span + (unit - first_unit(pt, worker));
+                                                 uint32_t unit, uint32_t head = 0) {
+  return (uint64_t(worker) * pt.max_span + (unit - first_unit(pt, worker))) * pt.heads + head;
+}
+
+// griddepcontrol: the partial pass lets the merge grid launch early; the
+// merge waits for the partial grid's completion (and memory) before reading.
+__device__ __forceinline__ void launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_primary() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // Record layout (fp32): [max: G][sum: G][out: G][D], padded to 4 floats.
@@ -95,11 +113,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
       reinterpret_cast<uint64_t *>(smem + WARPS * STAGES * Shape::kStageBytes) + warp * STAGES;
 
   const Partition pt = a.pt;
-  const uint32_t worker = blockIdx.x * WARPS + warp;
+  launch_dependents();
+  // heads == 1: this warp is a worker; otherwise the CTA is, and this warp
+  // serves kv head `warp` of each sequence in the CTA's range.
+  const bool grouped = pt.heads > 1;
+  const uint32_t worker = grouped ? blockIdx.x : blockIdx.x * WARPS + warp;
+  const uint32_t my_head = grouped ? uint32_t(warp) : 0u;
   const uint32_t total = pt.units * pt.tiles_per_unit;
   const uint32_t begin = min(total, worker * pt.tiles_per_worker);
   const uint32_t end = min(total, begin + pt.tiles_per_worker);
-  if (begin >= end)
+  if (begin >= end || (grouped && my_head >= pt.heads))
     return;  // warps are independent: no CTA-wide barrier below
 
   if (lane == 0) {
@@ -117,7 +140,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
   // are masked to -inf, so they contribute exactly zero).
   auto issue = [&](uint32_t tile, int stage) {
     const uint32_t unit = tile / tpu, key0 = (tile % tpu) * kTileKeys;
-    const uint32_t seq = unit / a.kv_heads, kvh = unit % a.kv_heads;
+    const uint32_t seq = grouped ? unit : unit / a.kv_heads;
+    const uint32_t kvh = grouped ? my_head : unit % a.kv_heads;
     const uint32_t valid = min(uint32_t(kTileKeys), a.keys - key0);
     if (lane == 0)
       mbar_arrive_expect_tx(&bars[stage], 2 * kTileKeys * Shape::kRowBytes);
@@ -149,7 +173,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
     l1 += __shfl_xor_sync(0xffffffffu, l1, 4);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 8);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 16);
-    float *rec = a.records + record_index(pt, worker, u) * a.record_floats;
+    float *rec = a.records + record_index(pt, worker, u, my_head) * a.record_floats;
     const uint32_t G = a.group;
     if (lane < 4) {
       if (head0 < G) {
@@ -189,7 +213,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
       if (unit != 0xffffffffu)
         flush(unit);
       unit = u;
-      const uint32_t seq = u / a.kv_heads, kvh = u % a.kv_heads;
+      const uint32_t seq = grouped ? u : u / a.kv_heads;
+      const uint32_t kvh = grouped ? my_head : u % a.kv_heads;
       const uint32_t head = lane >> 2;  // B operand column n = lane/4
       const __half *qrow = a.q + (size_t(seq) * a.kv_heads * a.group + kvh * a.group + head) * D;
 #pragma unroll
@@ -344,32 +369,52 @@ __global__ void __launch_bounds__(128) partial_simt(const Args a) {
   }
 }
 
-// Merge pass: one CTA per unit combines the records of every worker that
-// touched it and writes the group's fp16 outputs.
-__global__ void __launch_bounds__(256) merge(const Args a) {
+// Merge pass: one CTA per (sequence, kv head) combines the records of every
+// worker that touched it and writes the group's fp16 outputs.  Phase 1 (one
+// thread per query head) finds the global maximum and the normaliser;
+// phase 2 (one thread per output element) sums the rescaled partial outputs
+// with independent loads.  Launched as a programmatic dependent of the
+// partial pass: it may start while that grid drains and waits for it here.
+constexpr int kMergeThreads = 256;
+constexpr int kMergeMaxGroup = 64;
+
+__global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
+  __shared__ float s_top[kMergeMaxGroup], s_inv[kMergeMaxGroup];
   const Partition pt = a.pt;
-  const uint32_t unit = blockIdx.x;
-  if (unit >= pt.units)
-    return;
-  const uint32_t seq = unit / a.kv_heads, kvh = unit % a.kv_heads;
+  const uint32_t out_unit = blockIdx.x;  // seq * kv_heads + kvh
+  const uint32_t seq = out_unit / a.kv_heads, kvh = out_unit % a.kv_heads;
+  const bool grouped = pt.heads > 1;
+  const uint32_t unit = grouped ? seq : out_unit, head = grouped ? kvh : 0u;
   const uint32_t G = a.group, D = a.head_dim;
   const uint32_t w_lo = uint32_t((uint64_t(unit) * pt.tiles_per_unit) / pt.tiles_per_worker);
   const uint32_t w_hi =
       uint32_t((uint64_t(unit + 1) * pt.tiles_per_unit - 1) / pt.tiles_per_worker);
+  auto record = [&](uint32_t w) {
+    return a.records + record_index(pt, w, unit, head) * a.record_floats;
+  };
+  wait_primary();
+  for (uint32_t h = threadIdx.x; h < G; h += blockDim.x) {
+    float top = -INFINITY;
+    for (uint32_t w = w_lo; w <= w_hi; ++w)
+      top = fmaxf(top, record(w)[h]);
+    float sum = 0.f;
+    for (uint32_t w = w_lo; w <= w_hi; ++w)
+      sum = fmaf(record(w)[G + h], fast_exp2(record(w)[h] - top), sum);
+    s_top[h] = top;
+    s_inv[h] = 1.f / sum;
+  }
+  __syncthreads();
   __half *out = a.out + (size_t(seq) * a.kv_heads * G + kvh * G) * D;
   for (uint32_t i = threadIdx.x; i < G * D; i += blockDim.x) {
     const uint32_t h = i / D, d = i % D;
-    float top = -INFINITY;
-    for (uint32_t w = w_lo; w <= w_hi; ++w)
-      top = fmaxf(top, a.records[record_index(pt, w, unit) * a.record_floats + h]);
-    float sum = 0.f, acc = 0.f;
+    const float top = s_top[h];
+    float acc = 0.f;
+#pragma unroll 4
     for (uint32_t w = w_lo; w <= w_hi; ++w) {
-      const float *rec = a.records + record_index(pt, w, unit) * a.record_floats;
-      const float e = fast_exp2(rec[h] - top);
-      sum = fmaf(rec[G + h], e, sum);
-      acc = fmaf(rec[2 * G + h * D + d], e, acc);
+      const float *rec = record(w);
+      acc = fmaf(rec[2 * G + h * D + d], fast_exp2(rec[h] - top), acc);
     }
-    out[h * D + d] = __float2half_rn(acc / sum);
+    out[h * D + d] = __float2half_rn(acc * s_inv[h]);
   }
 }
 

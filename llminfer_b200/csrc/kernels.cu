@@ -11,7 +11,10 @@
 #include "delta_recurrent.cuh"
 #include "gqa_decode.cuh"
 #include "gqa_flash_simt.cuh"
+#include "gqa_prefill_tc.cuh"
 #include "host/status.h"
+
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cmath>
@@ -30,29 +33,35 @@ cudaStream_t as_stream(void *stream) { return static_cast<cudaStream_t>(stream);
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Opts a kernel in to more than 48 KiB of dynamic shared memory, once per
-// (kernel, device).
+// Raises a kernel's dynamic shared-memory limit to at least `bytes` on the
+// current device; the largest limit set so far is remembered per
+// (kernel, device) so the driver call is made only when it grows.
 int allow_smem(const void *kernel, size_t bytes, const DeviceInfo &dev) {
+  struct Entry {
+    const void *kernel;
+    int device;
+    size_t bytes;
+  };
   static std::mutex mutex;
-  static std::vector<std::pair<const void *, uint64_t>> done;  // kernel -> device bits
+  static std::vector<Entry> granted;
   if (bytes > dev.max_smem_optin)
     return fail(LLMI_UNSUPPORTED, "kernel needs %zu B of shared memory, device allows %zu", bytes,
                 dev.max_smem_optin);
   std::lock_guard<std::mutex> lock(mutex);
-  const uint64_t bit = uint64_t(1) << dev.device;
-  for (auto &entry : done)
-    if (entry.first == kernel && (entry.second & bit))
-      return LLMI_OK;
+  Entry *entry = nullptr;
+  for (auto &e : granted)
+    if (e.kernel == kernel && e.device == dev.device)
+      entry = &e;
+  if (entry && entry->bytes >= bytes)
+    return LLMI_OK;
   if (int s = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               int(bytes)),
                          "cudaFuncSetAttribute"))
     return s;
-  for (auto &entry : done)
-    if (entry.first == kernel) {
-      entry.second |= bit;
-      return LLMI_OK;
-    }
-  done.emplace_back(kernel, bit);
+  if (entry)
+    entry->bytes = bytes;
+  else
+    granted.push_back({kernel, dev.device, bytes});
   return LLMI_OK;
 }
 
@@ -119,22 +128,28 @@ int plan_decode(const llmi_gqa_params &p, unsigned batch, bool aligned, const De
       warps = kWarps64;
       smem = decode::MmaShape<64, kWarps64, kStages64>::kSmemBytes;
     }
+    // When the kv heads match the warps of a CTA, the CTA is the worker and
+    // its warps stream the same key rows of all kv heads (whole cache rows).
+    const bool grouped = p.kvHeads == uint32_t(warps);
+    const uint32_t part_units = grouped ? batch : units;
+    const uint32_t per_cta = grouped ? 1u : uint32_t(warps);
     const uint32_t tpu = (keys + decode::kTileKeys - 1) / decode::kTileKeys;
-    const uint64_t tiles = uint64_t(units) * tpu;
+    const uint64_t tiles = uint64_t(part_units) * tpu;
     if (tiles > UINT32_MAX)
       return fail(LLMI_UNSUPPORTED, "decode: %llu key tiles exceed 32 bits",
                   (unsigned long long)tiles);
-    const uint64_t workers_max = uint64_t(dev.sm_count) * warps;
+    const uint64_t workers_max = uint64_t(dev.sm_count) * per_cta;
     const uint32_t tpw = uint32_t((tiles + workers_max - 1) / workers_max);
     const uint32_t busy = uint32_t((tiles + tpw - 1) / tpw);
-    plan.grid = (busy + warps - 1) / warps;
+    plan.grid = (busy + per_cta - 1) / per_cta;
     plan.threads = warps * 32;
     plan.smem = size_t(smem);
-    plan.pt.units = units;
+    plan.pt.units = part_units;
     plan.pt.tiles_per_unit = tpu;
     plan.pt.tiles_per_worker = tpw;
-    plan.pt.max_span = std::min<uint32_t>(units, (tpw + tpu - 1) / tpu + 1);
-    plan.pt.workers = plan.grid * warps;
+    plan.pt.max_span = std::min<uint32_t>(part_units, (tpw + tpu - 1) / tpu + 1);
+    plan.pt.workers = plan.grid * per_cta;
+    plan.pt.heads = grouped ? p.kvHeads : 1u;
   } else {
     if (D > 512)
       return fail(LLMI_UNSUPPORTED, "decode: head_dim %u above 512", D);
@@ -146,12 +161,109 @@ int plan_decode(const llmi_gqa_params &p, unsigned batch, bool aligned, const De
     plan.pt.tiles_per_worker = 1;
     plan.pt.max_span = 1;
     plan.pt.workers = units * splits;
+    plan.pt.heads = 1;
     plan.grid = plan.pt.workers;
     plan.threads = 128;
     plan.smem = 0;
   }
-  plan.workspace = size_t(plan.pt.workers) * plan.pt.max_span * plan.record_floats * sizeof(float);
+  if (G > uint32_t(decode::kMergeMaxGroup))
+    return fail(LLMI_UNSUPPORTED, "decode: %u query heads per kv head (at most %d)", G,
+                decode::kMergeMaxGroup);
+  plan.workspace = size_t(plan.pt.workers) * plan.pt.max_span * plan.pt.heads *
+                   plan.record_floats * sizeof(float);
   return LLMI_OK;
+}
+
+// ---- TMA tensor maps ----------------------------------------------------------
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library does not link libcuda directly.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult result;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &result) !=
+            cudaSuccess ||
+        result != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// 4-D fp16 tensor map with 128-byte swizzle and zero fill out of bounds.
+// dims/box innermost first; strides in bytes for dims 1..3.
+int encode_map_4d(CUtensorMap *map, const void *base, const uint64_t (&dims)[4],
+                  const uint64_t (&strides)[3], const uint32_t (&box)[4]) {
+  auto encode = tensor_map_encoder();
+  if (!encode)
+    return fail(LLMI_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t s[3] = {strides[0], strides[1], strides[2]};
+  cuuint32_t b[4] = {box[0], box[1], box[2], box[3]};
+  cuuint32_t e[4] = {1, 1, 1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(base), d,
+                            s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(LLMI_CUDA_ERROR, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return LLMI_OK;
+}
+
+// The tensor-core prefill applies to head_dim 256 with a query group that
+// divides the 128-row tile, 16-byte aligned operands and cache strides.
+bool prefill_tc_fits(const llmi_gqa_params &p, unsigned batch, const void *q, const void *k,
+                     const void *v, size_t cache_stride, const void *out) {
+  const uint32_t G = p.queryHeads / p.kvHeads;
+  return p.headDim == uint32_t(prefill_tc::kD) && G <= uint32_t(prefill_tc::kRows) &&
+         prefill_tc::kRows % G == 0 && aligned16(q) && aligned16(k) && aligned16(v) &&
+         aligned16(out) && (batch == 1 || cache_stride % 8 == 0) && batch <= 65535 &&
+         p.kvHeads <= 65535;
+}
+
+int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *q,
+                      const uint16_t *k, const uint16_t *v, size_t cache_stride, uint16_t *out,
+                      const DeviceInfo &dev, cudaStream_t stream) {
+  using namespace prefill_tc;
+  const uint32_t G = p.queryHeads / p.kvHeads;
+  const uint32_t rows = p.past + p.tokens;
+  const uint64_t D = kD;
+  CUtensorMap mq, mk, mv;
+  // q [batch][tokens][Hq][D]: box = 64 dims x G heads x 128/G tokens.
+  {
+    const uint64_t dims[4] = {D, p.queryHeads, p.tokens, batch};
+    const uint64_t strides[3] = {D * 2, uint64_t(p.queryHeads) * D * 2,
+                                 uint64_t(p.tokens) * p.queryHeads * D * 2};
+    const uint32_t box[4] = {64, G, uint32_t(kRows) / G, 1};
+    if (int s = encode_map_4d(&mq, q, dims, strides, box))
+      return s;
+  }
+  // caches [batch][rows][Hkv][D] at sequence stride cache_stride: box = 64 dims x 1 head x 64 keys.
+  {
+    const uint64_t seq_bytes = batch > 1 ? uint64_t(cache_stride) * 2 : uint64_t(rows) * p.kvHeads * D * 2;
+    const uint64_t dims[4] = {D, p.kvHeads, rows, batch};
+    const uint64_t strides[3] = {D * 2, uint64_t(p.kvHeads) * D * 2, seq_bytes};
+    const uint32_t box[4] = {64, 1, uint32_t(kKeys), 1};
+    if (int s = encode_map_4d(&mk, k, dims, strides, box))
+      return s;
+    if (int s = encode_map_4d(&mv, v, dims, strides, box))
+      return s;
+  }
+  Args a;
+  a.out = reinterpret_cast<__half *>(out);
+  a.tokens = p.tokens;
+  a.q_heads = p.queryHeads;
+  a.kv_heads = p.kvHeads;
+  a.group = G;
+  a.past = p.past;
+  a.tok_per_tile = kRows / G;
+  a.tiles_per_head = (p.tokens + a.tok_per_tile - 1) / a.tok_per_tile;
+  a.scale_log2 = kLog2e / std::sqrt(float(kD));
+  if (int s = allow_smem(reinterpret_cast<const void *>(attend), Smem::alloc, dev))
+    return s;
+  dim3 grid(a.tiles_per_head, p.kvHeads, batch);
+  attend<<<grid, kThreads, Smem::alloc, stream>>>(mq, mk, mv, a);
+  return launched("gqaFlashAttention (tensor cores)");
 }
 
 template <int D, int WARPS, int STAGES>
@@ -202,6 +314,9 @@ extern "C" int llmi_cuda_gqa_prefill(const llmi_gqa_params *p, unsigned batch,
   DeviceInfo dev;
   if (int s = current_device(dev))
     return s;
+  if (prefill_tc_fits(*p, batch, q, k_cache, v_cache, cache_stride, out))
+    return launch_prefill_tc(*p, batch, q, k_cache, v_cache, cache_stride, out, dev,
+                             as_stream(stream));
   if (p->headDim > flash_simt::kMaxPerLane * 32)
     return fail(LLMI_UNSUPPORTED, "gqaFlashAttention: head_dim %u above 256", p->headDim);
   if (batch > 65535 || p->queryHeads > 65535)
@@ -308,7 +423,19 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
   }
   if (status)
     return status;
-  decode::merge<<<plan.pt.units, 256, 0, s>>>(a);
+  // The merge is a programmatic dependent of the partial pass: it may be
+  // scheduled while the partial grid drains and waits for it on the device.
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(batch * p->kvHeads);
+  config.blockDim = dim3(decode::kMergeThreads);
+  config.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  if (int e = check_cuda(cudaLaunchKernelEx(&config, decode::merge, a), "gqaSoftmax (decode merge)"))
+    return e;
   return launched("gqaSoftmax (decode merge)");
 }
 

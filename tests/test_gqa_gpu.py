@@ -55,6 +55,10 @@ def test_prefill_known_answers(case):
     (2, 33, 17, 8, 2, 64),
     (2, 5, 0, 4, 4, 128),
     (3, 70, 130, 16, 4, 256),
+    (2, 300, 0, 16, 4, 256),   # many key tiles: running-max rescales, stage reuse
+    (2, 40, 10, 8, 1, 256),    # group of 8 (16 tokens per tile)
+    (2, 50, 3, 4, 4, 256),     # group of 1 (128 tokens per tile)
+    (1, 7, 0, 32, 2, 256),     # group of 16, single partial tile
     (2, 19, 3, 4, 2, 12),      # odd head_dim (CUDA-core path)
     (1, 9, 40, 6, 2, 40),
 ])
@@ -103,8 +107,7 @@ def test_decode_and_prefill_agree_on_one_token():
 
 def test_decode_rejects_small_workspace():
     q, k, v = _inputs.gqa_case(2, 1, 100, 16, 4, 256, seed=13)
-    need = ops.decode_workspace_bytes(2, 16, 4, 256, 100)
-    small = torch.empty(need - 16, dtype=torch.uint8, device="cuda")
+    small = torch.empty(256, dtype=torch.uint8, device="cuda")
     with pytest.raises(abi.LlmiError) as err:
         ops.gqa_decode(dev(q), dev(k), dev(v), 100, workspace=small)
     assert err.value.status == abi.LLMI_WORKSPACE_TOO_SMALL
