@@ -47,7 +47,16 @@ def test_prefill_known_answers(case):
     torch.cuda.synchronize()
     got = out.double().cpu().numpy()
     expected = kat[f"case{case}_expected"].reshape(1, T, Hq, D)
-    assert np.all(np.abs(got - expected) <= 2e-4 + 5e-4 * np.abs(expected))
+    if D % 16:
+        # CUDA-core path, fp32 probabilities: the reference's own tolerance.
+        atol = 2e-4
+    else:
+        # Tensor-core path: P enters the P.V MMA rounded to fp16 (relative
+        # error <= 2^-11 per probability), so |error| <= 2^-11 * max|v|
+        # (= 9.8e-4 for these inputs, |v| <= 2) on top of the output rounding
+        # already covered by the 5e-4|e| term.
+        atol = 2.0 ** -11 * np.abs(kat[f"case{case}_v"].view(np.float16)).max() + 2e-5
+    assert np.all(np.abs(got - expected) <= atol + 5e-4 * np.abs(expected))
 
 
 @pytest.mark.parametrize("batch,tokens,past,hq,hkv,d", [
