@@ -108,6 +108,31 @@ int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch,
                          uint16_t *out, void *workspace,
                          size_t workspace_bytes, void *stream);
 
+/* Decode without a caller-provided workspace.  This entry point has no
+ * counterpart in the reference.  It exists for callers that cannot allocate
+ * device memory: an executor that hands out all device memory from its own
+ * fixed arena and allows no other allocation, or a latency-critical decode
+ * loop that cannot absorb the device-wide synchronisation cudaMalloc may
+ * imply.  It computes exactly what llmi_cuda_gqa_decode computes, using as
+ * scratch a fixed 8 MiB device array inside the library (held by every GPU
+ * that loads the library until the process exits).  It allocates nothing and
+ * frees nothing.
+ *  - Shapes whose scratch would exceed 8 MiB are rejected with
+ *    LLMI_WORKSPACE_TOO_SMALL before anything is launched; use
+ *    llmi_cuda_gqa_decode for those.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - All calls share the one array, and it keeps the previous call's
+ *    contents.  Nothing in it needs to start at zero: every record the merge
+ *    pass reads is written earlier in the same call.
+ *  - Calls that overlap on the GPU (for instance on two streams) race on the
+ *    array; serialise them. */
+int llmi_cuda_gqa_decode_noalloc(const llmi_gqa_params *p, unsigned batch,
+                                 const uint16_t *q, const uint16_t *k_cache,
+                                 const uint16_t *v_cache, size_t cache_stride,
+                                 uint16_t *out, void *stream);
+
 /* DeltaUpdate: graphDeltaUpdate (lib/Backend/Metal/Kernels/Graph.metal:146-170
  * with updateDeltaColumn, Reference.metal:182-197; operand contract
  * lib/GraphIR/Graph.cpp:226-246).  Per sequence:

@@ -439,6 +439,70 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
   return launched("gqaSoftmax (decode merge)");
 }
 
+// ---- decode without a caller workspace ------------------------------------------------
+//
+// For callers that cannot allocate device memory themselves: an executor that
+// hands out all device memory from its own fixed arena and forbids any other
+// allocation, or a latency-critical decode loop that cannot absorb the
+// device-wide synchronisation cudaMalloc may imply.  The scratch lives in
+// this fixed array instead; every GPU that loads the library holds it until
+// the process exits.
+
+constexpr size_t kStaticDecodeScratchBytes = size_t(8) << 20;  // 8 MiB
+
+static __device__ __align__(256) unsigned char g_static_decode_scratch[kStaticDecodeScratchBytes];
+
+namespace {
+
+// Device address of the static scratch on the current device.  The symbol's
+// host-side name is not a device address, so it is looked up once per device
+// with cudaGetSymbolAddress while that device is current, and cached.
+int static_decode_scratch(const DeviceInfo &dev, void **address) {
+  static std::mutex mutex;
+  static void *cached[64] = {};
+  std::lock_guard<std::mutex> lock(mutex);
+  if (!cached[dev.device]) {
+    void *p = nullptr;
+    if (int s = check_cuda(cudaGetSymbolAddress(&p, g_static_decode_scratch),
+                           "cudaGetSymbolAddress(static decode scratch)"))
+      return s;
+    cached[dev.device] = p;
+  }
+  *address = cached[dev.device];
+  return LLMI_OK;
+}
+
+}  // namespace
+
+extern "C" int llmi_cuda_gqa_decode_noalloc(const llmi_gqa_params *p, unsigned batch,
+                                            const uint16_t *q, const uint16_t *k_cache,
+                                            const uint16_t *v_cache, size_t cache_stride,
+                                            uint16_t *out, void *stream) {
+  clear_error();
+  if (int s = check_gqa(p, batch, q, k_cache, v_cache, cache_stride, out))
+    return s;
+  if (p->tokens != 1)
+    return fail(LLMI_UNSUPPORTED, "decode_noalloc: %u tokens; decode takes one token", p->tokens);
+  DeviceInfo dev;
+  if (int s = current_device(dev))
+    return s;
+  const bool aligned = aligned16(q) && aligned16(k_cache) && aligned16(v_cache) &&
+                       (batch == 1 || cache_stride % 8 == 0);
+  DecodePlan plan;
+  if (int s = plan_decode(*p, batch, aligned, dev, plan))
+    return s;
+  if (plan.workspace > kStaticDecodeScratchBytes)
+    return fail(LLMI_WORKSPACE_TOO_SMALL,
+                "decode_noalloc: this shape needs %zu B of scratch, the static scratch holds %zu B "
+                "(call llmi_cuda_gqa_decode with a workspace instead)",
+                plan.workspace, kStaticDecodeScratchBytes);
+  void *scratch = nullptr;
+  if (int s = static_decode_scratch(dev, &scratch))
+    return s;
+  return llmi_cuda_gqa_decode(p, batch, q, k_cache, v_cache, cache_stride, out, scratch,
+                              kStaticDecodeScratchBytes, stream);
+}
+
 // ---- graphDeltaUpdate ----------------------------------------------------------------
 
 extern "C" int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch, const float *q,
