@@ -89,6 +89,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
   }
 }
 
+// Bounded wait for kernels whose roles depend on one another: it also gives
+// up as soon as another role has set the CTA's abort flag, and a wait that
+// times out sets that flag, so every role leaves its loop.
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, unsigned parity,
+                                              volatile uint32_t *abort) {
+  if (mbar_try_wait(bar, parity))
+    return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity))
+        return true;
+    if (*abort)
+      return false;
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      raise_error(kErrWaitTimeout);
+      *abort = 1u;
+      return false;
+    }
+  }
+}
+
 // ---- bulk copies (TMA engine, no multicast) ----------------------------------
 
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
@@ -170,6 +192,23 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA/ALU pipes (no MUFU), for finite x; results are meant to be
+// rounded to fp16 afterwards.  Range reduction x = n + f with n = round(x)
+// (adding 1.5*2^23 rounds to an integer held in the low mantissa bits) and
+// f in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose coefficients were
+// fitted for this library (iteratively reweighted least squares for minimum
+// relative error on [-1/2, 1/2]): max relative error 7.5e-5, below fp16's
+// 2^-11 rounding.  2^n is applied by adding n to the exponent field.  x is
+// clamped to [-125, 126] so the result stays a normal float.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fminf(fmaxf(x, -125.f), 126.f);
+  const float shifter = 12582912.f;  // 1.5 * 2^23
+  const float t = x + shifter;
+  const float f = x - (t - shifter);
+  const float p = fmaf(fmaf(fmaf(0.05517132f, f, 0.24261054f), f, 0.69326099f), f, 0.99992811f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 }  // namespace llmi

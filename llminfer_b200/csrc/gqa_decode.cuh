@@ -6,16 +6,23 @@
 // (Reference.metal:303-323), gqaSoftmax (Graph.metal:172-210) and gqaValue
 // (Graph.metal:212-230).  Here the cache is streamed exactly once:
 //
-//  * The key range of every (sequence, kv head) "unit" is cut into tiles of
-//    16 keys, and the tiles of all units are laid end to end and divided
-//    evenly among "workers" (warps).  A worker streams its tiles through its
-//    own bulk-copy pipeline, keeps an online softmax for the GQA group of its
-//    unit, and writes one partial record (max, sum, unnormalised output) for
-//    every unit it touches.  Because whole tiles are balanced across warps,
-//    every SM streams the same number of bytes whatever the batch and
-//    context length.
-//  * The merge pass combines the records of each unit (log-sum-exp) and
-//    writes the fp16 output.
+//  * The key range of every unit is cut into tiles of 16 keys, and the tiles
+//    of all units are laid end to end and divided evenly among workers.  A
+//    worker keeps an online softmax for the GQA group of its unit and writes
+//    one partial record (max, sum, unnormalised output) for every unit it
+//    touches.  Because whole tiles are balanced across workers, every SM
+//    streams the same number of bytes whatever the batch and context length.
+//  * The merge pass combines the records of each (sequence, kv head)
+//    (log-sum-exp) and writes the fp16 output.
+//
+// Three partial-pass kernels:
+//  * partial_rows: a worker is a CTA and a unit a sequence.  A producer warp
+//    fetches whole cache rows (all kv heads of one key, 2 KiB for Hkv 4 x
+//    D 256) with one bulk copy each into a CTA-wide ring; warp h computes kv
+//    head h.  Used when Hkv * D * 2 == 2048.
+//  * partial_mma: a worker is a warp (or, when Hkv equals the warps of a CTA,
+//    the CTA) with private per-warp pipelines of 512-byte row copies.
+//  * partial_simt: CUDA cores, any head_dim <= 512 and any group.
 //
 // Scores and the softmax stay in fp32 (log2 domain).  Probabilities enter the
 // P.V product rounded to fp16, as in the reference's decode path.
@@ -42,9 +49,7 @@ constexpr int kTileKeys = 16;
 // Two shapes of worker:
 //  * heads == 1: a worker is one warp and a unit is one (sequence, kv head);
 //  * heads == Hkv: a worker is one CTA whose warp h serves kv head h, and a
-//    unit is one sequence.  The CTA's warps then stream the same key rows of
-//    every kv head together, so each 2 KiB cache row [Hkv][D] is fetched as a
-//    whole by one SM at one time.
+//    unit is one sequence.
 // Records are laid out [worker][span][heads].
 struct Partition {
   uint32_t units;             // sequences * (kv heads when heads == 1)
@@ -64,6 +69,11 @@ __host__ __device__ inline uint64_t record_index(const Partition &pt, uint32_t w
   return (uint64_t(worker) * pt.max_span + (unit - first_unit(pt, worker))) * pt.heads + head;
 }
 
+// Record layout (fp32): [max: G][sum: G][out: G][D], padded to 4 floats.
+__host__ __device__ inline uint32_t record_floats(uint32_t group, uint32_t head_dim) {
+  return (2 * group + group * head_dim + 3) & ~3u;
+}
+
 // griddepcontrol: the partial pass lets the merge grid launch early; the
 // merge waits for the partial grid's completion (and memory) before reading.
 __device__ __forceinline__ void launch_dependents() {
@@ -71,11 +81,6 @@ __device__ __forceinline__ void launch_dependents() {
 }
 __device__ __forceinline__ void wait_primary() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
-// Record layout (fp32): [max: G][sum: G][out: G][D], padded to 4 floats.
-__host__ __device__ inline uint32_t record_floats(uint32_t group, uint32_t head_dim) {
-  return (2 * group + group * head_dim + 3) & ~3u;
 }
 
 struct Args {
@@ -90,6 +95,228 @@ struct Args {
   float scale_log2;      // log2(e) / sqrt(D)
 };
 
+// One warp's tensor-core state for one unit: the group's queries as B
+// fragments, the running max / sum for its two heads (N columns
+// 2*(lane%4), +1) and the O^T accumulator fragments.
+template <int D>
+struct TileMath {
+  static constexpr int KS = D / 16;
+  uint32_t qf[KS][2];
+  float o[KS][4];
+  float m0, m1, l0, l1;
+
+  __device__ __forceinline__ void start(const __half *qgroup, uint32_t group, int lane) {
+    const uint32_t head = lane >> 2, head0 = (lane & 3) * 2;
+    const __half *qrow = qgroup + size_t(head) * D;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      if (head < group) {
+        qf[ks][0] = *reinterpret_cast<const uint32_t *>(qrow + ks * 16 + head0);
+        qf[ks][1] = *reinterpret_cast<const uint32_t *>(qrow + ks * 16 + head0 + 8);
+      } else {
+        qf[ks][0] = qf[ks][1] = 0u;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        o[ks][i] = 0.f;
+    }
+    m0 = m1 = -INFINITY;
+    l0 = l1 = 0.f;
+  }
+
+  // One 16-key tile.  kbase/vbase: shared addresses of key row 0 of this
+  // head's K and V slices; rows `row_stride` bytes apart; `valid` keys.
+  __device__ __forceinline__ void tile(uint32_t kbase, uint32_t vbase, uint32_t row_stride,
+                                       uint32_t valid, float scale_log2, int lane) {
+    const uint32_t krow = lane >> 2;
+    const uint32_t k_lane = ((lane & 7) + ((lane >> 3) & 1) * 8) * row_stride + (lane >> 4) * 16;
+    const uint32_t v_lane = ((lane & 7) + (lane >> 4) * 8) * row_stride + ((lane >> 3) & 1) * 16;
+    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < KS; ks += 2) {
+      uint32_t fa[4];
+      ldmatrix_x4(fa, kbase + k_lane + ks * 32);
+      mma_f16_16816(sa, fa, qf[ks][0], qf[ks][1]);
+      if (ks + 1 < KS) {
+        uint32_t fb[4];
+        ldmatrix_x4(fb, kbase + k_lane + (ks + 1) * 32);
+        mma_f16_16816(sb, fb, qf[ks + 1][0], qf[ks + 1][1]);
+      }
+    }
+    const float x0 = krow < valid ? (sa[0] + sb[0]) * scale_log2 : -INFINITY;
+    const float x1 = krow < valid ? (sa[1] + sb[1]) * scale_log2 : -INFINITY;
+    const float x2 = krow + 8 < valid ? (sa[2] + sb[2]) * scale_log2 : -INFINITY;
+    const float x3 = krow + 8 < valid ? (sa[3] + sb[3]) * scale_log2 : -INFINITY;
+    float t0 = fmaxf(x0, x2), t1 = fmaxf(x1, x3);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
+      t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
+    }
+    const float n0 = fmaxf(m0, t0), n1 = fmaxf(m1, t1);
+    const float r0 = fast_exp2(m0 - n0), r1 = fast_exp2(m1 - n1);
+    m0 = n0;
+    m1 = n1;
+    const float p0 = fast_exp2(x0 - n0), p1 = fast_exp2(x1 - n1);
+    const float p2 = fast_exp2(x2 - n0), p3 = fast_exp2(x3 - n1);
+    l0 = l0 * r0 + p0 + p2;
+    l1 = l1 * r1 + p1 + p3;
+    const uint32_t b0 = movmatrix_trans(pack_half2(p0, p1));
+    const uint32_t b1 = movmatrix_trans(pack_half2(p2, p3));
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+      o[mt][0] *= r0;
+      o[mt][1] *= r1;
+      o[mt][2] *= r0;
+      o[mt][3] *= r1;
+      uint32_t fv[4];
+      ldmatrix_x4_trans(fv, vbase + v_lane + mt * 32);
+      mma_f16_16816(o[mt], fv, b0, b1);
+    }
+  }
+
+  // Writes this unit's record (max and sum per head, O^T as [head][D]).
+  __device__ __forceinline__ void flush(float *rec, uint32_t G, int lane) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 4);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 8);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 16);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 4);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 8);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 16);
+    const uint32_t head0 = (lane & 3) * 2, krow = lane >> 2;
+    if (lane < 4) {
+      if (head0 < G) {
+        rec[head0] = m0;
+        rec[G + head0] = l0;
+      }
+      if (head0 + 1 < G) {
+        rec[head0 + 1] = m1;
+        rec[G + head0 + 1] = l1;
+      }
+    }
+    float *out0 = rec + 2 * G + head0 * D;
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+      const uint32_t d = mt * 16 + krow;
+      if (head0 < G) {
+        out0[d] = o[mt][0];
+        out0[d + 8] = o[mt][2];
+      }
+      if (head0 + 1 < G) {
+        out0[D + d] = o[mt][1];
+        out0[D + d + 8] = o[mt][3];
+      }
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// partial_rows: CTA-wide ring of whole cache rows, one producer warp.
+
+template <int D, int HKV, int STAGES>
+struct RowShape {
+  static constexpr int kRowBytes = HKV * D * 2;       // one key's [Hkv][D] row
+  static constexpr int kRowStride = kRowBytes + 16;   // +16 B: conflict-free ldmatrix per head
+  static constexpr int kTileBytes = kTileKeys * kRowStride;
+  static constexpr int kStageBytes = 2 * kTileBytes;  // K tile + V tile
+  static constexpr int kThreads = (HKV + 1) * 32;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + 2 * STAGES * 8 + 16;
+};
+
+template <int D, int HKV, int STAGES>
+__global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
+    partial_rows(const Args a) {
+  using Shape = RowShape<D, HKV, STAGES>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * Shape::kStageBytes);
+  uint64_t *empty = full + STAGES;
+  volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(empty + STAGES);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Partition pt = a.pt;  // heads == HKV, units = sequences
+  launch_dependents();
+  const uint32_t worker = blockIdx.x;
+  const uint32_t total = pt.units * pt.tiles_per_unit;
+  const uint32_t begin = min(total, worker * pt.tiles_per_worker);
+  const uint32_t end = min(total, begin + pt.tiles_per_worker);
+  if (begin >= end)
+    return;  // uniform over the CTA
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], HKV);
+    }
+    *abort = 0u;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const uint32_t tpu = pt.tiles_per_unit;
+
+  if (warp == HKV) {
+    // Producer: lanes 0-15 fetch the tile's 16 key rows, lanes 16-31 its 16
+    // value rows, each row [Hkv][D] with one bulk copy.  Rows past the end of
+    // the cache range repeat the last valid row (masked to -inf).
+    const uint64_t policy = policy_evict_first();
+    uint32_t issued = 0;
+    for (uint32_t t = begin; t < end; ++t) {
+      const uint32_t j = t - begin;
+      const int s = j % STAGES;
+      if (j >= STAGES &&
+          !__all_sync(0xffffffffu, wait_or_abort(&empty[s], ((j / STAGES) - 1) & 1, abort)))
+        break;
+      const uint32_t seq = t / tpu, key0 = (t % tpu) * kTileKeys;
+      const uint32_t valid = min(uint32_t(kTileKeys), a.keys - key0);
+      if (lane == 0)
+        mbar_arrive_expect_tx(&full[s], 2 * kTileKeys * Shape::kRowBytes);
+      __syncwarp();
+      const uint32_t row = lane & 15;
+      const uint32_t key = key0 + min(row, valid - 1);
+      const __half *src = (lane < 16 ? a.k : a.v) + seq * a.cache_stride + size_t(key) * HKV * D;
+      uint8_t *dst = smem + s * Shape::kStageBytes + (lane < 16 ? 0 : Shape::kTileBytes) +
+                     row * Shape::kRowStride;
+      bulk_g2s(dst, src, Shape::kRowBytes, &full[s], policy);
+      issued = j + 1;
+    }
+    // Every issued copy lands before the CTA can exit (bounded).
+    if (lane == 0)
+      for (uint32_t j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
+        mbar_wait(&full[j % STAGES], (j / STAGES) & 1);
+    __syncwarp();
+    return;
+  }
+
+  // Consumer warp: kv head `warp`.
+  const uint32_t h = warp;
+  TileMath<D> math;
+  uint32_t unit = 0xffffffffu;
+  bool ok = true;
+  for (uint32_t t = begin; t < end; ++t) {
+    const uint32_t j = t - begin;
+    const int s = j % STAGES;
+    const uint32_t u = t / tpu;
+    if (u != unit) {
+      if (unit != 0xffffffffu)
+        math.flush(a.records + record_index(pt, worker, unit, h) * a.record_floats, a.group, lane);
+      unit = u;
+      math.start(a.q + (size_t(u) * HKV * a.group + h * a.group) * D, a.group, lane);
+    }
+    if (!__all_sync(0xffffffffu, wait_or_abort(&full[s], (j / STAGES) & 1, abort))) {
+      ok = false;
+      break;
+    }
+    const uint32_t kbase = smem_u32(smem + s * Shape::kStageBytes) + h * D * 2;
+    const uint32_t valid = min(uint32_t(kTileKeys), a.keys - (t % tpu) * kTileKeys);
+    math.tile(kbase, kbase + Shape::kTileBytes, Shape::kRowStride, valid, a.scale_log2, lane);
+    __syncwarp();
+    if (lane == 0)
+      mbar_arrive(&empty[s]);
+  }
+  if (ok)
+    math.flush(a.records + record_index(pt, worker, unit, h) * a.record_floats, a.group, lane);
+}
+
+// ---------------------------------------------------------------------------
+// partial_mma: per-warp pipelines of 512-byte row copies.
+
 template <int D, int WARPS, int STAGES>
 struct MmaShape {
   static constexpr int kRowBytes = D * 2;
@@ -99,13 +326,10 @@ struct MmaShape {
   static constexpr int kSmemBytes = WARPS * STAGES * kStageBytes + WARPS * STAGES * 8;
 };
 
-// Partial pass on tensor cores.  One CTA per SM; each warp is a worker with a
-// private STAGES-deep pipeline of 16-key tiles.  Requires D % 16 == 0,
-// D <= 256 and group <= 8.
+// Requires D % 16 == 0, D <= 256 and group <= 8.
 template <int D, int WARPS, int STAGES>
 __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
   using Shape = MmaShape<D, WARPS, STAGES>;
-  constexpr int KS = D / 16;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t *stages = smem + warp * STAGES * Shape::kStageBytes;
@@ -159,50 +383,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
     if (begin + s < end)
       issue(begin + s, s);
 
-  const uint32_t head0 = (lane & 3) * 2;  // this lane's two heads (N columns)
-  const uint32_t krow = lane >> 2;        // this lane's key rows: krow, krow+8
+  TileMath<D> math;
   uint32_t unit = 0xffffffffu;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  float o[KS][4];
-  uint32_t qf[KS][2];
-
-  auto flush = [&](uint32_t u) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 4);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 8);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 16);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 4);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 8);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 16);
-    float *rec = a.records + record_index(pt, worker, u, my_head) * a.record_floats;
-    const uint32_t G = a.group;
-    if (lane < 4) {
-      if (head0 < G) {
-        rec[head0] = m0;
-        rec[G + head0] = l0;
-      }
-      if (head0 + 1 < G) {
-        rec[head0 + 1] = m1;
-        rec[G + head0 + 1] = l1;
-      }
-    }
-    float *out0 = rec + 2 * G + head0 * D;
-#pragma unroll
-    for (int mt = 0; mt < KS; ++mt) {
-      const uint32_t d = mt * 16 + krow;
-      if (head0 < G) {
-        out0[d] = o[mt][0];
-        out0[d + 8] = o[mt][2];
-      }
-      if (head0 + 1 < G) {
-        out0[D + d] = o[mt][1];
-        out0[D + d + 8] = o[mt][3];
-      }
-    }
-  };
-
-  const uint32_t k_lane = ((lane & 7) + ((lane >> 3) & 1) * 8) * Shape::kRowStride + (lane >> 4) * 16;
-  const uint32_t v_lane = ((lane & 7) + (lane >> 4) * 8) * Shape::kRowStride + ((lane >> 3) & 1) * 16;
-
   uint32_t t = begin;
   bool ok = true;
   for (; t < end; ++t) {
@@ -211,88 +393,27 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
     const uint32_t u = t / tpu;
     if (u != unit) {
       if (unit != 0xffffffffu)
-        flush(unit);
+        math.flush(a.records + record_index(pt, worker, unit, my_head) * a.record_floats, a.group,
+                   lane);
       unit = u;
       const uint32_t seq = grouped ? u : u / a.kv_heads;
       const uint32_t kvh = grouped ? my_head : u % a.kv_heads;
-      const uint32_t head = lane >> 2;  // B operand column n = lane/4
-      const __half *qrow = a.q + (size_t(seq) * a.kv_heads * a.group + kvh * a.group + head) * D;
-#pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        if (head < a.group) {
-          qf[ks][0] = *reinterpret_cast<const uint32_t *>(qrow + ks * 16 + head0);
-          qf[ks][1] = *reinterpret_cast<const uint32_t *>(qrow + ks * 16 + head0 + 8);
-        } else {
-          qf[ks][0] = qf[ks][1] = 0u;
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o[ks][i] = 0.f;
-      }
-      m0 = m1 = -INFINITY;
-      l0 = l1 = 0.f;
+      math.start(a.q + (size_t(seq) * a.kv_heads * a.group + kvh * a.group) * D, a.group, lane);
     }
-
     ok = __all_sync(0xffffffffu, mbar_wait(&bars[stage], (j / STAGES) & 1));
     if (!ok)
       break;
-
     const uint32_t kbase = smem_u32(stages + stage * Shape::kStageBytes);
-    const uint32_t vbase = kbase + Shape::kTileBytes;
     const uint32_t valid = min(uint32_t(kTileKeys), a.keys - (t % tpu) * kTileKeys);
-
-    // S^T = K Q^T for 16 keys x 8 heads; two accumulators for ILP.
-    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int ks = 0; ks < KS; ks += 2) {
-      uint32_t fa[4];
-      ldmatrix_x4(fa, kbase + k_lane + ks * 32);
-      mma_f16_16816(sa, fa, qf[ks][0], qf[ks][1]);
-      if (ks + 1 < KS) {
-        uint32_t fb[4];
-        ldmatrix_x4(fb, kbase + k_lane + (ks + 1) * 32);
-        mma_f16_16816(sb, fb, qf[ks + 1][0], qf[ks + 1][1]);
-      }
-    }
-    float x0 = krow < valid ? (sa[0] + sb[0]) * a.scale_log2 : -INFINITY;
-    float x1 = krow < valid ? (sa[1] + sb[1]) * a.scale_log2 : -INFINITY;
-    float x2 = krow + 8 < valid ? (sa[2] + sb[2]) * a.scale_log2 : -INFINITY;
-    float x3 = krow + 8 < valid ? (sa[3] + sb[3]) * a.scale_log2 : -INFINITY;
-
-    float t0 = fmaxf(x0, x2), t1 = fmaxf(x1, x3);
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
-      t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
-    }
-    const float n0 = fmaxf(m0, t0), n1 = fmaxf(m1, t1);
-    const float r0 = fast_exp2(m0 - n0), r1 = fast_exp2(m1 - n1);
-    m0 = n0;
-    m1 = n1;
-    const float p0 = fast_exp2(x0 - n0), p1 = fast_exp2(x1 - n1);
-    const float p2 = fast_exp2(x2 - n0), p3 = fast_exp2(x3 - n1);
-    l0 = l0 * r0 + p0 + p2;
-    l1 = l1 * r1 + p1 + p3;
-
-    const uint32_t b0 = movmatrix_trans(pack_half2(p0, p1));
-    const uint32_t b1 = movmatrix_trans(pack_half2(p2, p3));
-#pragma unroll
-    for (int mt = 0; mt < KS; ++mt) {
-      o[mt][0] *= r0;
-      o[mt][1] *= r1;
-      o[mt][2] *= r0;
-      o[mt][3] *= r1;
-      uint32_t fv[4];
-      ldmatrix_x4_trans(fv, vbase + v_lane + mt * 32);
-      mma_f16_16816(o[mt], fv, b0, b1);
-    }
+    math.tile(kbase, kbase + Shape::kTileBytes, Shape::kRowStride, valid, a.scale_log2, lane);
     __syncwarp();  // every lane is done with this stage before it is refilled
     if (t + STAGES < end)
       issue(t + STAGES, stage);
   }
 
   if (ok) {
-    flush(unit);
+    math.flush(a.records + record_index(pt, worker, unit, my_head) * a.record_floats, a.group,
+               lane);
     return;
   }
   // A wait gave up: let the copies already issued land (bounded) before the
@@ -303,8 +424,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
   }
 }
 
-// Partial pass for shapes outside the tensor-core kernel (any head_dim up to
+// ---------------------------------------------------------------------------
+// partial_simt: shapes outside the tensor-core kernels (any head_dim up to
 // 512, any group).  One CTA per (unit, key split); warps take query heads.
+
 __global__ void __launch_bounds__(128) partial_simt(const Args a) {
   constexpr int kMaxPerLane = 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -369,17 +492,18 @@ __global__ void __launch_bounds__(128) partial_simt(const Args a) {
   }
 }
 
-// Merge pass: one CTA per (sequence, kv head) combines the records of every
-// worker that touched it and writes the group's fp16 outputs.  Phase 1 (one
-// thread per query head) finds the global maximum and the normaliser;
-// phase 2 (one thread per output element) sums the rescaled partial outputs
-// with independent loads.  Launched as a programmatic dependent of the
-// partial pass: it may start while that grid drains and waits for it here.
-constexpr int kMergeThreads = 256;
+// ---------------------------------------------------------------------------
+// Merge pass: one CTA per (sequence, kv head), one warp per query head.  The
+// warp reads every record's max and sum in parallel (lane i: record i),
+// reduces them with shuffles, then each lane sums its output dimensions over
+// the records with independent, coalesced loads.  Launched as a programmatic
+// dependent of the partial pass: it may start while that grid drains and
+// waits for it here.
+constexpr int kMergeThreads = 128;
 constexpr int kMergeMaxGroup = 64;
+constexpr int kMergeMaxPerLane = 16;  // head_dim <= 512
 
 __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
-  __shared__ float s_top[kMergeMaxGroup], s_inv[kMergeMaxGroup];
   const Partition pt = a.pt;
   const uint32_t out_unit = blockIdx.x;  // seq * kv_heads + kvh
   const uint32_t seq = out_unit / a.kv_heads, kvh = out_unit % a.kv_heads;
@@ -389,32 +513,51 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   const uint32_t w_lo = uint32_t((uint64_t(unit) * pt.tiles_per_unit) / pt.tiles_per_worker);
   const uint32_t w_hi =
       uint32_t((uint64_t(unit + 1) * pt.tiles_per_unit - 1) / pt.tiles_per_worker);
-  auto record = [&](uint32_t w) {
-    return a.records + record_index(pt, w, unit, head) * a.record_floats;
+  const uint32_t n = w_hi - w_lo + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto record = [&](uint32_t i) {
+    return a.records + record_index(pt, w_lo + i, unit, head) * a.record_floats;
   };
   wait_primary();
-  for (uint32_t h = threadIdx.x; h < G; h += blockDim.x) {
-    float top = -INFINITY;
-    for (uint32_t w = w_lo; w <= w_hi; ++w)
-      top = fmaxf(top, record(w)[h]);
-    float sum = 0.f;
-    for (uint32_t w = w_lo; w <= w_hi; ++w)
-      sum = fmaf(record(w)[G + h], fast_exp2(record(w)[h] - top), sum);
-    s_top[h] = top;
-    s_inv[h] = 1.f / sum;
-  }
-  __syncthreads();
   __half *out = a.out + (size_t(seq) * a.kv_heads * G + kvh * G) * D;
-  for (uint32_t i = threadIdx.x; i < G * D; i += blockDim.x) {
-    const uint32_t h = i / D, d = i % D;
-    const float top = s_top[h];
-    float acc = 0.f;
-#pragma unroll 4
-    for (uint32_t w = w_lo; w <= w_hi; ++w) {
-      const float *rec = record(w);
-      acc = fmaf(rec[2 * G + h * D + d], fast_exp2(rec[h] - top), acc);
+  for (uint32_t h = warp; h < G; h += kMergeThreads / 32) {
+    float top = -INFINITY;
+    for (uint32_t i = lane; i < n; i += 32)
+      top = fmaxf(top, record(i)[h]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+      top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, off));
+    float sum = 0.f;
+    for (uint32_t i = lane; i < n; i += 32) {
+      const float *r = record(i);
+      sum = fmaf(r[G + h], fast_exp2(r[h] - top), sum);
     }
-    out[h * D + d] = __float2half_rn(acc * s_inv[h]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+      sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    float acc[kMergeMaxPerLane];
+#pragma unroll
+    for (int k = 0; k < kMergeMaxPerLane; ++k)
+      acc[k] = 0.f;
+#pragma unroll 2
+    for (uint32_t i = 0; i < n; ++i) {
+      const float *r = record(i);
+      const float w = fast_exp2(r[h] - top);
+      const float *o = r + 2 * G + h * D;
+#pragma unroll
+      for (int k = 0; k < kMergeMaxPerLane; ++k) {
+        const uint32_t d = lane + 32 * k;
+        if (d < D)
+          acc[k] = fmaf(o[d], w, acc[k]);
+      }
+    }
+    const float inv = 1.f / sum;
+#pragma unroll
+    for (int k = 0; k < kMergeMaxPerLane; ++k) {
+      const uint32_t d = lane + 32 * k;
+      if (d < D)
+        out[h * D + d] = __float2half_rn(acc[k] * inv);
+    }
   }
 }
 

@@ -32,7 +32,7 @@ inline size_t smem_bytes(uint32_t D) {
   return sizeof(float) * (size_t(kKeys) * (D + 1) + size_t(kKeys) * D + size_t(kWarps) * D);
 }
 
-__global__ void __launch_bounds__(kWarps * 32) attend(const Args a) {
+__global__ void __launch_bounds__(kWarps * 32) gqa_prefill_simt(const Args a) {
   extern __shared__ float sm[];
   const uint32_t D = a.head_dim, ldk = D + 1;
   float *ks = sm;

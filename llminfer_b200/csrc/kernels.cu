@@ -91,7 +91,7 @@ int check_gqa(const llmi_gqa_params *p, unsigned batch, const void *q, const voi
 // ---- decode planning -------------------------------------------------------
 
 struct DecodePlan {
-  enum Kind { Mma256, Mma128, Mma64, Simt } kind = Simt;
+  enum Kind { Rows256x4, Rows128x8, Mma256, Mma128, Mma64, Simt } kind = Simt;
   decode::Partition pt{};
   uint32_t record_floats = 0;
   uint32_t grid = 0, threads = 0;
@@ -102,6 +102,7 @@ struct DecodePlan {
 constexpr int kWarps256 = 4, kStages256 = 3;
 constexpr int kWarps128 = 8, kStages128 = 3;
 constexpr int kWarps64 = 8, kStages64 = 4;
+constexpr int kRowStages = 3;
 
 // Picks the decode kernels and the work partition.  The tensor-core partial
 // pass needs 16-byte aligned operands (bulk copies) and a supported shape;
@@ -113,7 +114,33 @@ int plan_decode(const llmi_gqa_params &p, unsigned batch, bool aligned, const De
   const uint32_t units = batch * p.kvHeads;
   plan.record_floats = decode::record_floats(G, D);
   const bool fits = G <= 8 && (D == 256 || D == 128 || D == 64);
-  if (fits && aligned) {
+  const bool rows = fits && aligned && ((D == 256 && p.kvHeads == 4) || (D == 128 && p.kvHeads == 8));
+  if (rows) {
+    // Whole 2 KiB cache rows per bulk copy; the CTA is the worker.
+    if (D == 256) {
+      plan.kind = DecodePlan::Rows256x4;
+      plan.threads = decode::RowShape<256, 4, kRowStages>::kThreads;
+      plan.smem = decode::RowShape<256, 4, kRowStages>::kSmemBytes;
+    } else {
+      plan.kind = DecodePlan::Rows128x8;
+      plan.threads = decode::RowShape<128, 8, kRowStages>::kThreads;
+      plan.smem = decode::RowShape<128, 8, kRowStages>::kSmemBytes;
+    }
+    const uint32_t tpu = (keys + decode::kTileKeys - 1) / decode::kTileKeys;
+    const uint64_t tiles = uint64_t(batch) * tpu;
+    if (tiles > UINT32_MAX)
+      return fail(LLMI_UNSUPPORTED, "decode: %llu key tiles exceed 32 bits",
+                  (unsigned long long)tiles);
+    const uint64_t workers_max = uint64_t(dev.sm_count);
+    const uint32_t tpw = uint32_t((tiles + workers_max - 1) / workers_max);
+    plan.grid = uint32_t((tiles + tpw - 1) / tpw);
+    plan.pt.units = batch;
+    plan.pt.tiles_per_unit = tpu;
+    plan.pt.tiles_per_worker = tpw;
+    plan.pt.max_span = std::min<uint32_t>(batch, (tpw + tpu - 1) / tpu + 1);
+    plan.pt.workers = plan.grid;
+    plan.pt.heads = p.kvHeads;
+  } else if (fits && aligned) {
     int warps, smem;
     if (D == 256) {
       plan.kind = DecodePlan::Mma256;
@@ -228,16 +255,7 @@ int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *
   const uint32_t G = p.queryHeads / p.kvHeads;
   const uint32_t rows = p.past + p.tokens;
   const uint64_t D = kD;
-  CUtensorMap mq, mk, mv;
-  // q [batch][tokens][Hq][D]: box = 64 dims x G heads x 128/G tokens.
-  {
-    const uint64_t dims[4] = {D, p.queryHeads, p.tokens, batch};
-    const uint64_t strides[3] = {D * 2, uint64_t(p.queryHeads) * D * 2,
-                                 uint64_t(p.tokens) * p.queryHeads * D * 2};
-    const uint32_t box[4] = {64, G, uint32_t(kRows) / G, 1};
-    if (int s = encode_map_4d(&mq, q, dims, strides, box))
-      return s;
-  }
+  CUtensorMap mk, mv;
   // caches [batch][rows][Hkv][D] at sequence stride cache_stride: box = 64 dims x 1 head x 64 keys.
   {
     const uint64_t seq_bytes = batch > 1 ? uint64_t(cache_stride) * 2 : uint64_t(rows) * p.kvHeads * D * 2;
@@ -250,6 +268,7 @@ int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *
       return s;
   }
   Args a;
+  a.q = reinterpret_cast<const __half *>(q);
   a.out = reinterpret_cast<__half *>(out);
   a.tokens = p.tokens;
   a.q_heads = p.queryHeads;
@@ -259,11 +278,21 @@ int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *
   a.tok_per_tile = kRows / G;
   a.tiles_per_head = (p.tokens + a.tok_per_tile - 1) / a.tok_per_tile;
   a.scale_log2 = kLog2e / std::sqrt(float(kD));
-  if (int s = allow_smem(reinterpret_cast<const void *>(attend), Smem::alloc, dev))
+  if (int s = allow_smem(reinterpret_cast<const void *>(gqa_prefill_tcgen05), Smem::alloc, dev))
     return s;
   dim3 grid(a.tiles_per_head, p.kvHeads, batch);
-  attend<<<grid, kThreads, Smem::alloc, stream>>>(mq, mk, mv, a);
+  gqa_prefill_tcgen05<<<grid, kThreads, Smem::alloc, stream>>>(mk, mv, a);
   return launched("gqaFlashAttention (tensor cores)");
+}
+
+template <int D, int HKV, int STAGES>
+int launch_decode_rows(const DecodePlan &plan, const decode::Args &args, const DeviceInfo &dev,
+                       cudaStream_t stream) {
+  auto kernel = decode::partial_rows<D, HKV, STAGES>;
+  if (int s = allow_smem(reinterpret_cast<const void *>(kernel), plan.smem, dev))
+    return s;
+  kernel<<<plan.grid, plan.threads, plan.smem, stream>>>(args);
+  return launched("gqaScores (decode partial, row stream)");
 }
 
 template <int D, int WARPS, int STAGES>
@@ -335,10 +364,10 @@ extern "C" int llmi_cuda_gqa_prefill(const llmi_gqa_params *p, unsigned batch,
   a.group = p->queryHeads / p->kvHeads;
   a.scale_log2 = kLog2e / std::sqrt(float(p->headDim));
   const size_t smem = flash_simt::smem_bytes(p->headDim);
-  if (int s = allow_smem(reinterpret_cast<const void *>(flash_simt::attend), smem, dev))
+  if (int s = allow_smem(reinterpret_cast<const void *>(flash_simt::gqa_prefill_simt), smem, dev))
     return s;
   dim3 grid((p->tokens + flash_simt::kWarps - 1) / flash_simt::kWarps, p->queryHeads, batch);
-  flash_simt::attend<<<grid, flash_simt::kWarps * 32, smem, as_stream(stream)>>>(a);
+  flash_simt::gqa_prefill_simt<<<grid, flash_simt::kWarps * 32, smem, as_stream(stream)>>>(a);
   return launched("gqaFlashAttention (CUDA cores)");
 }
 
@@ -407,6 +436,12 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
   cudaStream_t s = as_stream(stream);
   int status = LLMI_OK;
   switch (plan.kind) {
+  case DecodePlan::Rows256x4:
+    status = launch_decode_rows<256, 4, kRowStages>(plan, a, dev, s);
+    break;
+  case DecodePlan::Rows128x8:
+    status = launch_decode_rows<128, 8, kRowStages>(plan, a, dev, s);
+    break;
   case DecodePlan::Mma256:
     status = launch_decode_mma<256, kWarps256, kStages256>(plan, a, dev, s);
     break;

@@ -86,6 +86,7 @@ def test_prefill_matches_dense_oracle(batch, tokens, past, hq, hkv, d):
     (2, 77, 8, 8, 128),
     (2, 300, 16, 2, 256),      # group of 8 query heads
     (2, 33, 8, 1, 64),
+    (2, 40, 16, 8, 64),        # CTA workers with per-warp pipelines
     (2, 50, 4, 2, 12),         # odd head_dim (CUDA-core path)
     (2, 20, 24, 2, 64),        # group of 12 (CUDA-core path)
 ])
