@@ -72,16 +72,12 @@ def load_peaks():
 
 def profile_traffic(name: str):
     """DRAM bytes per launch recorded in profiles/<name>.md ('traffic_bytes_per_launch: N')."""
+    import re
     path = ROOT / "profiles" / f"{name}.md"
     if not path.exists():
         return None
-    for line in path.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return int(line.split(":", 1)[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
+    match = re.search(r"traffic_bytes_per_launch:\s*(\d+)", path.read_text())
+    return int(match.group(1)) if match else None
 
 
 class ClockSampler:
