@@ -8,6 +8,7 @@
 
 #include "cache_append.cuh"
 #include "common.cuh"
+#include "delta_chunk.cuh"
 #include "delta_recurrent.cuh"
 #include "gqa_decode.cuh"
 #include "gqa_flash_simt.cuh"
@@ -103,6 +104,8 @@ constexpr int kWarps256 = 4, kStages256 = 3;
 constexpr int kWarps128 = 8, kStages128 = 3;
 constexpr int kWarps64 = 8, kStages64 = 4;
 constexpr int kRowStages = 3;
+// DeltaUpdate calls with at least this many tokens use the chunked kernel.
+constexpr uint32_t kChunkedMinTokens = 16;
 
 // Picks the decode kernels and the work partition.  The tensor-core partial
 // pass needs 16-byte aligned operands (bulk copies) and a supported shape;
@@ -568,6 +571,21 @@ extern "C" int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch
   a.value_dim = p->valueDim;
   a.group = p->valueHeads / p->keyHeads;
   cudaStream_t s = as_stream(stream);
+  // Multi-token calls: chunked form on tensor cores (dk = dv = 128).
+  const bool chunked = p->tokens >= kChunkedMinTokens && p->keyDim == 128 && p->valueDim == 128 &&
+                       aligned16(q) && aligned16(k) && aligned16(v) && aligned16(state) &&
+                       batch <= 65535 && p->valueHeads <= 2147483647u;
+  if (chunked) {
+    DeviceInfo dev;
+    if (int e = current_device(dev))
+      return e;
+    const size_t smem = delta_chunk::Smem::total;
+    if (int e = allow_smem(reinterpret_cast<const void *>(delta_chunk::chunked), smem, dev))
+      return e;
+    dim3 grid(p->valueHeads, batch);
+    delta_chunk::chunked<<<grid, delta_chunk::kThreads, smem, s>>>(a);
+    return launched("graphDeltaUpdate (chunked)");
+  }
   const bool fast = p->valueDim == 128 && (p->keyDim == 128 || p->keyDim == 64) &&
                     aligned16(state) && aligned16(v) && batch <= 65535 &&
                     p->valueHeads <= 2147483647u;
