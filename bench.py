@@ -19,7 +19,13 @@ Keys of the line beyond the base contract:
   e2e           the same step through the C-ABI calls with pinned host
                 buffers: H2D of q and the new rows, D2H of the output, timed
   secondary     the other kernels of the path on their benchmark configs
-                (C1 prefill, C4 DeltaNet step, C3 DeltaNet prefill)
+                (C1 prefill, C4 DeltaNet step, C3 DeltaNet prefill), each
+                run whole on every GPU (aggregate over N GPUs, max-over-ranks
+                time)
+  stack         the C5 hybrid stack (llminfer_b200/stack.py): 24 DeltaNet +
+                8 GQA layers, batch 16, prefill 8192 then 256 decode steps,
+                split by (sequence x head) over the N GPUs with an NCCL
+                all-gather of head outputs (strong scaling)
 `--impl reference` runs the reference arm: the CPU restatement of the
 reference's code (oracle/, "port") on the host cores, same metric.
 """
@@ -40,6 +46,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "GQA/DeltaNet attn TFLOP/s (prefill), HBM GB/s (decode) vs roofline, 1-8 GPU"
 C2 = dict(batch=64, past=4096, capacity=8192, query_heads=16, kv_heads=4, head_dim=256)
+# C5: the hybrid stack (24 DeltaNet + 8 GQA layers), a fixed job split over the GPUs.
+C5 = dict(batch=16, prefill=8192, decode=256, layers=32)
 FALLBACK_PEAKS = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
 SEED = 179531
 
@@ -51,6 +59,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-secondary", action="store_true", help="skip C1/C3/C4 measurements")
+    p.add_argument("--no-stack", action="store_true", help="skip the C5 hybrid-stack run")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     return p.parse_args()
 
@@ -353,10 +362,6 @@ def run_ours(args, dist):
     h2d = (q.numel() + kn.numel() + vn.numel()) * 2
     d2h = out.numel() * 2
 
-    secondary = []
-    if not args.no_secondary and dist.world == 1:
-        secondary = run_secondary(torch, ops, device, peaks)
-
     cpu = None
     if not args.no_cpu and dist.world == 1 and dist.rank == 0:
         gbs, secs, n, threads, flags = cpu_decode_sample(q, kc, vc, P)
@@ -364,6 +369,23 @@ def run_ours(args, dist):
                "sample": f"{n} of 64 sequences of the C2 decode step (CausalGqa), "
                          f"{secs:.1f} s; dense fp64 check of tests/FlashAttentionTest.mm:53-85 "
                          f"restated in oracle/oracle.c, gcc {flags} -fopenmp"}
+
+    del q, kn, vn, kc, vc, out, ws, hq, hk, hv, hout, dq, dk, dv
+    torch.cuda.empty_cache()
+    secondary = []
+    if not args.no_secondary:
+        secondary = run_secondary(torch, ops, device, peaks, dist)
+    stack = None
+    if not args.no_stack:
+        from llminfer_b200.stack import run_stack
+        dist.barrier()
+        stack = run_stack(torch, dist.pg, dist.world, dist.rank, **C5)
+        stack["prefill_frac_of_bf16_peak"] = round(
+            stack["prefill_tflops"] / dist.world / peaks["bf16_tflops"], 4)
+        stack["decode_frac_of_hbm_peak"] = round(
+            stack["decode_gbs"] / dist.world / peaks["hbm_gbs"], 4)
+        stack["scaling"] = "strong"
+        torch.cuda.empty_cache()
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": dist.world,
@@ -394,13 +416,17 @@ def run_ours(args, dist):
         "gpu_launches": 4 * K,
         "clocks": clocks.summary(),
         "secondary": secondary,
+        "stack": stack,
     }
     return line
 
 
-def time_op(torch, fn, reps=10, warmup=3):
+def time_op(torch, fn, dist, reps=10, warmup=3):
+    """Median and best CUDA-event time of fn (ms), max over ranks."""
     for _ in range(warmup):
         fn()
+    torch.cuda.synchronize()
+    dist.barrier()
     torch.cuda.synchronize()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(reps)]
@@ -410,26 +436,30 @@ def time_op(torch, fn, reps=10, warmup=3):
         b.record()
     torch.cuda.synchronize()
     t = sorted(a.elapsed_time(b) for a, b in evs)
-    return statistics.median(t), t[0]
+    return dist.max(statistics.median(t)), dist.max(t[0])
 
 
-def run_secondary(torch, ops, device, peaks):
-    """The other kernels of the path on their benchmark configs (CUDA events, median)."""
+def run_secondary(torch, ops, device, peaks, dist):
+    """The other kernels of the path on their benchmark configs (CUDA events, median,
+    max over ranks).  Every rank runs the whole config on its own GPU, so with N GPUs
+    the aggregate is N times the per-GPU work over the slowest rank's time."""
     g = torch.Generator(device=device)
-    g.manual_seed(SEED)
+    g.manual_seed(SEED + dist.rank)
+    N = dist.world
     res = []
     # C1: GQA prefill, B=1, T=128, past 0.
     q = torch.randn(1, 128, 16, 256, generator=g, device=device).half()
     kc = torch.randn(1, 128, 4, 256, generator=g, device=device).half()
     vc = torch.randn(1, 128, 4, 256, generator=g, device=device).half()
     out = torch.empty_like(q)
-    med, best = time_op(torch, lambda: ops.gqa_prefill(q, kc, vc, 0, out=out))
+    med, best = time_op(torch, lambda: ops.gqa_prefill(q, kc, vc, 0, out=out), dist)
     macs = step_bytes([1], 128, 0, 128, 1, query_heads=16, kv_heads=4, head_dim=256)["CausalGqa"][1]
     tf = 2 * macs / (med / 1e3) / 1e12
-    res.append({"workload": "C1 GQA prefill B=1 T=128 past 0 (gqaFlashAttention)",
-                "ms": round(med, 4), "value": round(tf, 3), "unit": "TFLOP/s",
+    res.append({"workload": "C1 GQA prefill B=1 T=128 past 0 (gqaFlashAttention)"
+                            + (f", {N} replicas" if N > 1 else ""),
+                "ms": round(med, 4), "value": round(tf * N, 3), "unit": "TFLOP/s",
                 "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4)})
-    # C4: DeltaNet recurrent step, B=256.
+    # C4: DeltaNet recurrent step, B=256 per GPU.
     B, Hk, dk, Hv, dv = 256, 16, 128, 32, 128
     qd = torch.nn.functional.normalize(torch.randn(B, 1, Hk, dk, generator=g, device=device), dim=-1)
     qd = (qd / dk ** 0.5).reshape(B, 1, Hk * dk).contiguous()
@@ -440,15 +470,16 @@ def run_secondary(torch, ops, device, peaks):
     decay = torch.exp(-torch.nn.functional.softplus(torch.randn(B, 1, Hv, generator=g, device=device)))
     state = torch.randn(B, Hv, dk, dv, generator=g, device=device) * 0.02
     od = torch.empty_like(vd)
-    med, best = time_op(torch, lambda: ops.delta_update(qd, kd, vd, beta, decay, state, out=od))
+    med, best = time_op(torch, lambda: ops.delta_update(qd, kd, vd, beta, decay, state, out=od),
+                        dist)
     nbytes = step_bytes([0], 1, 0, 1, B, key_heads=Hk, key_dim=dk, value_heads=Hv,
                         value_dim=dv)["DeltaUpdate"][0]
     gbs = nbytes / (med / 1e3) / 1e9
-    res.append({"workload": "C4 DeltaNet recurrent step B=256 (graphDeltaUpdate)",
-                "ms": round(med, 4), "value": round(gbs, 1), "unit": "GB/s",
+    res.append({"workload": f"C4 DeltaNet recurrent step B=256 per GPU (graphDeltaUpdate)",
+                "ms": round(med, 4), "value": round(gbs * N, 1), "unit": "GB/s",
                 "frac_of_hbm_peak": round(gbs / peaks["hbm_gbs"], 4)})
     del qd, kd, vd, beta, decay, state, od
-    # C3: DeltaNet prefill, B=4, T=4096.
+    # C3: DeltaNet prefill, B=4, T=4096 per GPU.
     B, T = 4, 4096
     qd = torch.nn.functional.normalize(torch.randn(B, T, Hk, dk, generator=g, device=device), dim=-1)
     qd = (qd / dk ** 0.5).reshape(B, T, Hk * dk).contiguous()
@@ -460,13 +491,14 @@ def run_secondary(torch, ops, device, peaks):
     state = torch.zeros(B, Hv, dk, dv, device=device)
     od = torch.empty_like(vd)
     med, best = time_op(torch, lambda: ops.delta_update(qd, kd, vd, beta, decay, state, out=od),
-                        reps=3, warmup=1)
+                        dist, reps=5, warmup=2)
     cost = step_bytes([0], T, 0, T, B, key_heads=Hk, key_dim=dk, value_heads=Hv,
                       value_dim=dv)["DeltaUpdate"]
-    res.append({"workload": "C3 DeltaNet prefill B=4 T=4096 (graphDeltaUpdate)",
-                "ms": round(med, 4), "value": round(cost[0] / (med / 1e3) / 1e9, 1),
-                "unit": "GB/s", "tflops_cost_model": round(2 * cost[1] / (med / 1e3) / 1e12, 3),
-                "frac_of_hbm_peak": round(cost[0] / (med / 1e3) / 1e9 / peaks["hbm_gbs"], 4)})
+    gbs = cost[0] / (med / 1e3) / 1e9
+    res.append({"workload": "C3 DeltaNet prefill B=4 T=4096 per GPU (graphDeltaUpdate, chunked)",
+                "ms": round(med, 4), "value": round(gbs * N, 1), "unit": "GB/s",
+                "tflops_cost_model": round(2 * cost[1] * N / (med / 1e3) / 1e12, 3),
+                "frac_of_hbm_peak": round(gbs / peaks["hbm_gbs"], 4)})
     return res
 
 

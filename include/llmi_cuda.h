@@ -216,6 +216,14 @@ int llmi_cuda_session_enqueue(llmi_session *session, unsigned tokens,
  * the session becomes invalid. */
 int llmi_cuda_session_sync(llmi_session *session);
 
+/* Registers one cudaEvent_t per layer (count == layers; events == NULL with
+ * count 0 clears them).  During step/enqueue the session records events[l]
+ * on its stream right after the last launch of layer l, so a caller can
+ * start a per-layer collective on another stream (cudaStreamWaitEvent) while
+ * the following layers compute.  The events are borrowed, not destroyed. */
+int llmi_cuda_session_set_layer_events(llmi_session *session,
+                                       void *const *events, unsigned count);
+
 /* MetalSession::reset (MetalExecutor.mm:294-298): zero all states, past = 0,
  * clear the invalid mark. */
 int llmi_cuda_session_reset(llmi_session *session);

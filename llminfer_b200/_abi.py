@@ -82,6 +82,7 @@ SIGNATURES = [
     ("llmi_cuda_session_step", c_int, [c_void_p, c_uint, POINTER(LayerIO), c_int]),
     ("llmi_cuda_session_enqueue", c_int, [c_void_p, c_uint, POINTER(LayerIO)]),
     ("llmi_cuda_session_sync", c_int, [c_void_p]),
+    ("llmi_cuda_session_set_layer_events", c_int, [c_void_p, POINTER(c_void_p), c_uint]),
     ("llmi_cuda_session_reset", c_int, [c_void_p]),
     ("llmi_cuda_session_past", c_uint64, [c_void_p]),
     ("llmi_cuda_session_is_invalid", c_int, [c_void_p]),

@@ -38,6 +38,7 @@ struct llmi_session {
   uint64_t past = 0;
   bool invalid = false;
   std::string plan;
+  std::vector<cudaEvent_t> layerEvents;  // borrowed; recorded after each layer
 
   ~llmi_session() {
     for (auto *list : {&keys, &values, &recurrent})
@@ -171,6 +172,10 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
     }
     if (e)
       return e;
+    if (!s.layerEvents.empty() && (i + 1 == ops.size() || ops[i + 1].layer != op.layer))
+      if (int st = check_cuda(cudaEventRecord(s.layerEvents[op.layer], s.stream),
+                              "record layer event"))
+        return st;
     if (trace)
       for (size_t d = next; d < next + count && d < dispatches.size(); ++d) {
         char line[160];
@@ -280,6 +285,28 @@ extern "C" int llmi_cuda_session_sync(llmi_session *s) {
     s->invalid = true;
     return e;
   }
+  return LLMI_OK;
+}
+
+extern "C" int llmi_cuda_session_set_layer_events(llmi_session *s, void *const *events,
+                                                  unsigned count) {
+  clear_error();
+  if (!s)
+    return fail(LLMI_INVALID_ARGUMENT, "set_layer_events: null session");
+  if (count == 0 && !events) {
+    s->layerEvents.clear();
+    return LLMI_OK;
+  }
+  if (!events || count != s->config.kinds.size())
+    return fail(LLMI_INVALID_ARGUMENT, "set_layer_events: %u events for %zu layers", count,
+                s->config.kinds.size());
+  std::vector<cudaEvent_t> list(count);
+  for (unsigned l = 0; l < count; ++l) {
+    if (!events[l])
+      return fail(LLMI_INVALID_ARGUMENT, "set_layer_events: event %u is null", l);
+    list[l] = static_cast<cudaEvent_t>(events[l]);
+  }
+  s->layerEvents = std::move(list);
   return LLMI_OK;
 }
 

@@ -183,6 +183,17 @@ class AttentionSession:
     def reset(self) -> None:
         check(lib.llmi_cuda_session_reset(self._handle))
 
+    def set_layer_events(self, events) -> None:
+        """Record events[l] on the session stream after layer l of every step
+        (None clears).  Events must already exist (recorded once)."""
+        if events is None:
+            check(lib.llmi_cuda_session_set_layer_events(self._handle, None, 0))
+            self._layer_events = None
+            return
+        handles = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+        check(lib.llmi_cuda_session_set_layer_events(self._handle, handles, len(events)))
+        self._layer_events = list(events)  # keep them alive while registered
+
     def _sync_inputs(self) -> None:
         # Operands produced on torch's current stream must be ready before the
         # session stream reads them.
