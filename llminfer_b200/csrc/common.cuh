@@ -111,6 +111,27 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, unsigned parity,
   }
 }
 
+// ---- cp.async -----------------------------------------------------------------
+
+// cp.async of 16 (or 4) bytes global -> shared; `bytes_valid` 0 writes zeros
+// without reading.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t bytes_valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(bytes_valid)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src, uint32_t bytes_valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(bytes_valid)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // ---- bulk copies (TMA engine, no multicast) ----------------------------------
 
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
@@ -191,6 +212,13 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// log2(x) for x > 0, subnormal inputs included (MUFU approximation).
+__device__ __forceinline__ float fast_log2(float x) {
+  float y;
+  asm("lg2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 

@@ -8,7 +8,7 @@
 
 #include "cache_append.cuh"
 #include "common.cuh"
-#include "delta_chunk.cuh"
+#include "delta_chunk_tc.cuh"
 #include "delta_recurrent.cuh"
 #include "gqa_decode.cuh"
 #include "gqa_flash_simt.cuh"
@@ -234,6 +234,27 @@ int encode_map_4d(CUtensorMap *map, const void *base, const uint64_t (&dims)[4],
   cuuint32_t e[4] = {1, 1, 1, 1};
   const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(base), d,
                             s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(LLMI_CUDA_ERROR, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return LLMI_OK;
+}
+
+// 3-D tensor map (no swizzle: row-major staging), zero fill out of bounds.
+// dims/box innermost first; strides in bytes for dims 1..2.
+int encode_map_3d(CUtensorMap *map, CUtensorMapDataType type, const void *base,
+                  const uint64_t (&dims)[3], const uint64_t (&strides)[2],
+                  const uint32_t (&box)[3],
+                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
+  auto encode = tensor_map_encoder();
+  if (!encode)
+    return fail(LLMI_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t s[2] = {strides[0], strides[1]};
+  cuuint32_t b[3] = {box[0], box[1], box[2]};
+  cuuint32_t e[3] = {1, 1, 1};
+  const CUresult r = encode(map, type, 3, const_cast<void *>(base), d, s, b, e,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(LLMI_CUDA_ERROR, "cuTensorMapEncodeTiled failed (%d)", int(r));
@@ -574,17 +595,45 @@ extern "C" int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch
   // Multi-token calls: chunked form on tensor cores (dk = dv = 128).
   const bool chunked = p->tokens >= kChunkedMinTokens && p->keyDim == 128 && p->valueDim == 128 &&
                        aligned16(q) && aligned16(k) && aligned16(v) && aligned16(state) &&
-                       batch <= 65535 && p->valueHeads <= 2147483647u;
+                       aligned16(out) && batch <= 65535 && p->valueHeads <= 2147483647u;
   if (chunked) {
     DeviceInfo dev;
     if (int e = current_device(dev))
       return e;
-    const size_t smem = delta_chunk::Smem::total;
-    if (int e = allow_smem(reinterpret_cast<const void *>(delta_chunk::chunked), smem, dev))
+    // q, k fp32 [batch][tokens][keyHeads * 128]: a box is the 64 rows x 128
+    // columns of one head's chunk.  v and out fp16 [batch][tokens][valueHeads * 128]:
+    // v in two 128B-swizzled boxes of 64 columns (the MMA operand layout), out
+    // written from a row-major tile.
+    CUtensorMap mq, mk, mv, mo;
+    const uint64_t kw = uint64_t(p->keyHeads) * 128, vw = uint64_t(p->valueHeads) * 128;
+    const uint64_t T = p->tokens;
+    const uint32_t C = delta_tc::C;
+    {
+      const uint64_t dims[3] = {kw, T, batch};
+      const uint64_t strides[2] = {kw * 4, T * kw * 4};
+      const uint32_t box[3] = {128, C, 1};
+      if (int e = encode_map_3d(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, q, dims, strides, box))
+        return e;
+      if (int e = encode_map_3d(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, k, dims, strides, box))
+        return e;
+    }
+    {
+      const uint64_t dims[3] = {vw, T, batch};
+      const uint64_t strides[2] = {vw * 2, T * vw * 2};
+      const uint32_t vbox[3] = {64, C, 1};
+      if (int e = encode_map_3d(&mv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, v, dims, strides, vbox,
+                                CU_TENSOR_MAP_SWIZZLE_128B))
+        return e;
+      const uint32_t obox[3] = {128, C, 1};
+      if (int e = encode_map_3d(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, out, dims, strides, obox))
+        return e;
+    }
+    const size_t smem = delta_tc::Smem::total + 1024;
+    if (int e = allow_smem(reinterpret_cast<const void *>(delta_tc::chunked_tc), smem, dev))
       return e;
     dim3 grid(p->valueHeads, batch);
-    delta_chunk::chunked<<<grid, delta_chunk::kThreads, smem, s>>>(a);
-    return launched("graphDeltaUpdate (chunked)");
+    delta_tc::chunked_tc<<<grid, delta_tc::kThreads, smem, s>>>(mq, mk, mv, mo, a);
+    return launched("graphDeltaUpdate (chunked, tcgen05)");
   }
   const bool fast = p->valueDim == 128 && (p->keyDim == 128 || p->keyDim == 64) &&
                     aligned16(state) && aligned16(v) && batch <= 65535 &&

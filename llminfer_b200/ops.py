@@ -174,8 +174,15 @@ class AttentionSession:
         self._sync_inputs()
         check(lib.llmi_cuda_session_step(self._handle, tokens, self._io(layers), int(trace_plan)))
 
+    def operand_table(self, layers):
+        """The C operand table (llmi_layer_io[]) of `layers`.  It holds raw device
+        pointers: reusable for every step over the same buffers while they live."""
+        return self._io(layers)
+
     def enqueue(self, tokens: int, layers) -> None:
-        check(lib.llmi_cuda_session_enqueue(self._handle, tokens, self._io(layers)))
+        """Enqueue a step; `layers` is a list of LayerTensors or an operand_table()."""
+        table = layers if isinstance(layers, ctypes.Array) else self._io(layers)
+        check(lib.llmi_cuda_session_enqueue(self._handle, tokens, table))
 
     def sync(self) -> None:
         check(lib.llmi_cuda_session_sync(self._handle))

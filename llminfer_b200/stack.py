@@ -33,6 +33,7 @@ import json
 import math
 import os
 import statistics
+import time
 from dataclasses import dataclass
 
 LAYER_DELTANET, LAYER_GQA = 0, 1
@@ -209,6 +210,10 @@ class StackRun:
         # can run while step s is gathered.
         self.dec_out = [torch.empty(len(self.kinds), self.b, 1, self.width, dtype=torch.float16,
                                     device=self.device) for _ in range(2)]
+        # The decode steps reuse the same buffers: build their operand tables once.
+        self._dec_layers = [self._io(self.dec_in, [o[l] for l in range(len(self.kinds))])
+                            for o in self.dec_out]
+        self._dec_tables = [self.session.operand_table(x) for x in self._dec_layers]
         self.dec_free = [torch.cuda.Event() for _ in range(2)]
         for e in self.dec_free:
             e.record(self.comm)
@@ -265,7 +270,7 @@ class StackRun:
         buf = step & 1
         out = self.dec_out[buf]
         self.stream.wait_event(self.dec_free[buf])
-        self.session.enqueue(1, self._io(self.dec_in, [out[l] for l in range(len(self.kinds))]))
+        self.session.enqueue(1, self._dec_tables[buf])
         if self.gathering:
             self.comm.wait_event(self.events[-1])
             self._gather(self.dec_gathered, out)
@@ -337,7 +342,7 @@ def run_stack(torch, dist, world, rank, batch=16, prefill=8192, decode=256, laye
     run = StackRun(torch, kinds, batch, prefill, decode, shape, plan, dist=dist, seed=seed)
     try:
         run.warmup()
-        pre_ms, dec_ms = [], []
+        pre_ms, dec_ms, issue_ms = [], [], []
         for _ in range(repeats):
             if dist is not None and world > 1:
                 dist.barrier()
@@ -346,10 +351,12 @@ def run_stack(torch, dist, world, rank, batch=16, prefill=8192, decode=256, laye
             ev[0].record(run.stream)
             run.run_prefill()
             ev[1].record(run.stream)
+            t0 = time.perf_counter()
             for s in range(decode):
                 run.run_decode_step(s)
             run.join()
             ev[2].record(run.stream)
+            issue_ms.append((time.perf_counter() - t0) * 1e3)
             run.session.sync()
             torch.cuda.synchronize()
             p, d = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
@@ -378,6 +385,8 @@ def run_stack(torch, dist, world, rank, batch=16, prefill=8192, decode=256, laye
         "decode_ms": round(d, 3),
         "decode_tok_s": round(batch * decode / (d / 1e3), 1),
         "decode_gbs": round(costs["decode_bytes"] / (d / 1e3) / 1e9, 1),
+        # Host time to issue the decode steps (rank 0): near decode_ms means launch-bound.
+        "decode_host_issue_ms": round(statistics.median(issue_ms), 3),
         "repeats": repeats,
         "cost_model": {"prefill_gflop": round(2 * costs["prefill_macs"] / 1e9, 1),
                        "prefill_gqa_gflop": round(2 * costs["prefill_gqa_macs"] / 1e9, 1),
