@@ -143,8 +143,10 @@ int llmi_cuda_gqa_decode_noalloc(const llmi_gqa_params *p, unsigned batch,
  *   out:    [tokens][valueHeads*valueDim] fp16
  * For each token: S = decay*S; pred = S^T k; delta = beta*(v - pred);
  * S += k delta^T; y = S^T q.  Value head vh uses key head
- * vh / (valueHeads/keyHeads).  tokens == 1 runs the register-resident
- * recurrent step; tokens > 1 runs the chunked (chunk 64) form. */
+ * vh / (valueHeads/keyHeads).  Fewer than 16 tokens run the
+ * register-resident recurrent kernel token by token; 16 or more (with
+ * keyDim == valueDim == 128 and 16-byte aligned operands) run the chunked
+ * (chunk 64) form on the tensor cores, equal up to rounding. */
 int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch,
                            const float *q, const float *k, const uint16_t *v,
                            const float *beta, const float *decay, float *state,
