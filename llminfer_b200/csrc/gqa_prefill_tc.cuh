@@ -6,31 +6,30 @@
 // Tiling.  One CTA owns 128 query rows of one (sequence, kv head): the G
 // query heads of the group stacked over 128/G consecutive tokens
 // (row r = token (r / G), head (r % G)), so each K/V tile is fetched once for
-// the whole group.  Keys stream in tiles of 64.
+// the whole group.  Keys stream in tiles of 128, so S = Q K^T runs as
+// M128 N128 instructions: N = 64 instructions reach only ~70 % of the
+// tensor pipe's rate on sm_100, N >= 128 the full rate.
 //
-// Q lives in TMEM.  Both MMAs read their A operand from TMEM, so only K and
-// V cross shared memory: S_j = Q K_j^T as a TS MMA (M128 N64 K256) streams
-// 64 B of K per clock, where an SS form would stream Q too (192 B/clk, more
-// than shared memory feeds the tensor core).  This also frees the 64 KiB a
-// shared-memory Q tile would take for deeper K/V rings.
+// Operands.  Q (fp16, 64 KiB) sits in shared memory for the whole CTA, so
+// S = Q K^T is an SS MMA; with N = 128 its 8 KiB of operands per
+// instruction match what shared memory feeds the tensor core.  K streams
+// through a ring of 16 KiB boxes (128 keys x 64 dims), V through a ring of
+// 16 KiB groups (32 keys x 256 dims as four 64-dim boxes); each slot is
+// released as soon as the MMAs reading it retire.  O += P V is a TS MMA
+// (P from TMEM, V MN-major), M128 N256.
 //
 // Roles (320 threads, one CTA per SM):
 //   warps 0-7  softmax.  Warps w and w+4 share TMEM lanes 32*(w%4).. (query
-//              rows).  At the start each writes its half of the rows' Q into
-//              TMEM.  Per tile both read the row's 64 scores with tcgen05.ld
-//              and apply the causal mask, so both derive the same row maximum
-//              without exchanging it; after a pair barrier (both have read S)
-//              warp w exponentiates keys [0,32) and warp w+4 keys [32,64) and
-//              writes the probabilities as fp16 over the S buffer.  The row
-//              sums are combined once, in the epilogue, where each half
-//              normalises 128 of the 256 output columns.
-//   warp 8     TMA producer: K tiles into a 4-slot ring and V tiles into a
-//              3-slot ring, K one tile ahead.
-//   warp 9     TMEM allocator; one elected thread issues the MMAs:
-//                S_j = Q K_j^T     (TS: A = Q from TMEM, B = K K-major)
-//                O  += P_j V_j     (TS: A = P from TMEM, B = V MN-major)
-//              and commits them to mbarriers.
-// TMEM columns: O [0,256), Q [256,384), S/P buffers [384,448) and [448,512).
+//              rows); per tile warp w+4h reads keys [64h, 64h+64) of its
+//              rows, the pair exchanges row maxima through shared memory,
+//              and each warp writes its 64 probabilities as fp16 pairs over
+//              the S columns it read (after the exchange both have read).
+//              The row sums are combined once, in the epilogue, where each
+//              half normalises 128 of the 256 output columns.
+//   warp 8     TMA producer: Q once, then K one tile ahead of V.
+//   warp 9     TMEM allocator; one elected thread issues the MMAs and
+//              commits them to mbarriers.
+// TMEM columns: O [0,256), S/P buffers [256,384) and [384,512).
 //
 // Rescaling O.  The running maximum used for the exponentials only moves
 // when a row's tile maximum exceeds it by more than 8 (log2 units), so
@@ -55,40 +54,38 @@ namespace prefill_tc {
 
 constexpr int kD = 256;
 constexpr int kRows = 128;
-constexpr int kKeys = 64;
+constexpr int kKeys = 128;            // keys per tile
 constexpr int kSoftmaxWarps = 8;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 320;
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
-// Every kPolyEvery-th exponential of a fully visible tile runs on the FMA
-// pipe (exp2_fma) instead of MUFU; 0 disables it.
-constexpr int kPolyEvery = 0;
-constexpr int kKVBytes = kKeys * kD * 2;  // 32 KiB, 4 boxes of 8 KiB
-// K and V have separate rings: K_j is released as soon as S_j retires, V_j
-// after P_j V_j, so the K ring runs a tile ahead of V and the next S MMA
-// does not wait behind the previous P.V.
-constexpr int kKStages = 4;
-constexpr int kVStages = 3;
-constexpr int kSBuffers = 2;  // S/P buffers in TMEM
+constexpr int kBoxBytes = 16384;      // one K box (128 keys x 64 dims) or V group (32 keys x 256)
+constexpr int kKBoxesPerTile = kD / 64;
+constexpr int kVKeys = 32;            // keys per V group
+constexpr int kVGroupsPerTile = kKeys / kVKeys;
+constexpr int kKSlots = 5;
+constexpr int kVSlots = 4;
+constexpr int kSBuffers = 2;          // S/P buffers in TMEM
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 0, kColQ = 256, kColS = 384;
+constexpr uint32_t kColO = 0, kColS = 256;
 constexpr float kRescaleThreshold = 8.0f;
 
 struct Smem {
   // Offsets from the 1024-byte aligned base.
-  static constexpr int k = 0;
-  static constexpr int v = k + kKStages * kKVBytes;
-  static constexpr int bars = v + kVStages * kKVBytes;
-  static constexpr int row_sum = bars + 256;  // [2 halves][128 rows] fp32
+  static constexpr int q = 0;                              // 4 boxes [128 rows][64 dims]
+  static constexpr int k = q + kRows * kD * 2;
+  static constexpr int v = k + kKSlots * kBoxBytes;
+  static constexpr int bars = v + kVSlots * kBoxBytes;
+  static constexpr int row_max = bars + 256;               // [2 tiles][2 halves][128 rows] fp32
+  static constexpr int row_sum = row_max + 4 * kRows * 4;  // [2 halves][128 rows] fp32
   static constexpr int total = row_sum + 2 * kRows * 4;
   static constexpr int alloc = total + 1024;  // alignment slack
 };
 static_assert(Smem::alloc <= 232448, "shared memory budget of one sm_100 CTA");
 
 struct Args {
-  const __half *q;  // [batch][tokens][Hq][D]
-  __half *out;      // [batch][tokens][Hq][D]
+  __half *out;  // [batch][tokens][Hq][D]
   uint32_t tokens, q_heads, kv_heads, group, past, tok_per_tile, tiles_per_head;
   float scale_log2;
 };
@@ -107,26 +104,30 @@ __device__ __forceinline__ bool pair_sync(uint64_t *bar, unsigned parity,
   return ok;
 }
 
+// map_q: q [batch][tokens][Hq][D], box 64 dims x G heads x 128/G tokens;
+// map_k: cache [batch][rows][Hkv][D], box 64 dims x 1 head x 128 keys;
+// map_v: same cache layout, box 64 dims x 1 head x 32 keys; all 128B-swizzled.
 __global__ void __launch_bounds__(kThreads, 1)
-    gqa_prefill_tcgen05(const __grid_constant__ CUtensorMap map_k,
+    gqa_prefill_tcgen05(const __grid_constant__ CUtensorMap map_q,
+                        const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Smem::bars);
-  uint64_t *q_ready = bars + 0;     // Q written to TMEM (softmax threads)
-  uint64_t *bar_k = bars + 1;       // [kKStages] K tile landed
-  uint64_t *k_empty = bars + 5;     // [kKStages] S MMA done with the K slot
-  uint64_t *bar_v = bars + 9;       // [kVStages] V tile landed
-  uint64_t *v_empty = bars + 12;    // [kVStages] P.V MMA done with the V slot
-  uint64_t *s_full = bars + 15;     // [kSBuffers]
-  uint64_t *p_ready = bars + 17;    // [kSBuffers]
-  uint64_t *o_done = bars + 19;
-  uint64_t *o_final = bars + 20;
-  uint64_t *drain = bars + 21;
-  uint64_t *pair_bar = bars + 22;   // [4] softmax warp pairs
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 26);
-  volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(bars + 27);
+  uint64_t *q_full = bars + 0;      // Q landed
+  uint64_t *bar_k = bars + 1;       // [kKSlots] K box landed
+  uint64_t *k_empty = bars + 6;     // [kKSlots] S MMAs done with the K slot
+  uint64_t *bar_v = bars + 11;      // [kVSlots] V group landed
+  uint64_t *v_empty = bars + 15;    // [kVSlots] P.V MMAs done with the V slot
+  uint64_t *s_full = bars + 19;     // [kSBuffers]
+  uint64_t *p_ready = bars + 21;    // [kSBuffers]
+  uint64_t *o_done = bars + 23;
+  uint64_t *o_final = bars + 24;
+  uint64_t *drain = bars + 25;
+  uint64_t *pair_bar = bars + 26;   // [4] softmax warp pairs
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 30);
+  volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(bars + 31);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Heaviest (latest-token) tiles first.
@@ -137,12 +138,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t n_tiles = (a.past + t_last + 1 + kKeys - 1) / kKeys;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_ready, kSoftmaxThreads);
-    for (int s = 0; s < kKStages; ++s) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kKSlots; ++s) {
       mbar_init(&bar_k[s], 1);
       mbar_init(&k_empty[s], 1);
     }
-    for (int s = 0; s < kVStages; ++s) {
+    for (int s = 0; s < kVSlots; ++s) {
       mbar_init(&bar_v[s], 1);
       mbar_init(&v_empty[s], 1);
     }
@@ -158,13 +159,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort = 0u;
     fence_barrier_init();
   }
-  if (warp == kMmaWarp) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
+  if (warp == kMmaWarp)
+    tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -173,47 +169,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      prefetch_map(&map_q);
       prefetch_map(&map_k);
       prefetch_map(&map_v);
-      // Issue order K_0, then per tile j: K_{j+1}, V_j (K runs a tile ahead).
+      mbar_arrive_expect_tx(q_full, kRows * kD * 2);
+      for (int b = 0; b < kKBoxesPerTile; ++b)
+        tma_load_4d(smem + Smem::q + b * kBoxBytes, &map_q, b * 64, int(kvh * a.group), int(t0),
+                    int(seq), q_full);
+      // K boxes and V groups are numbered in issue order; box n uses slot
+      // n % slots in its (n / slots)-th round.  k_boxes / v_groups count the
+      // copies issued so far.
+      uint32_t k_boxes = 0, v_groups = 0;
       auto load_k = [&](uint32_t j) -> bool {
-        const int s = j % kKStages;
-        if (j >= kKStages && !wait_or_abort(&k_empty[s], ((j / kKStages) - 1) & 1, abort))
-          return false;
-        mbar_arrive_expect_tx(&bar_k[s], kKVBytes);
-        for (int b = 0; b < 4; ++b)
-          tma_load_4d(smem + Smem::k + s * kKVBytes + b * (kKVBytes / 4), &map_k, b * 64, int(kvh),
-                      int(j * kKeys), int(seq), &bar_k[s]);
+        for (int b = 0; b < kKBoxesPerTile; ++b) {
+          const uint32_t n = j * kKBoxesPerTile + b, s = n % kKSlots;
+          if (n >= kKSlots && !wait_or_abort(&k_empty[s], ((n / kKSlots) - 1) & 1, abort))
+            return false;
+          mbar_arrive_expect_tx(&bar_k[s], kBoxBytes);
+          tma_load_4d(smem + Smem::k + s * kBoxBytes, &map_k, b * 64, int(kvh), int(j * kKeys),
+                      int(seq), &bar_k[s]);
+          k_boxes = n + 1;
+        }
         return true;
       };
       auto load_v = [&](uint32_t j) -> bool {
-        const int s = j % kVStages;
-        if (j >= kVStages && !wait_or_abort(&v_empty[s], ((j / kVStages) - 1) & 1, abort))
-          return false;
-        mbar_arrive_expect_tx(&bar_v[s], kKVBytes);
-        for (int b = 0; b < 4; ++b)
-          tma_load_4d(smem + Smem::v + s * kKVBytes + b * (kKVBytes / 4), &map_v, b * 64, int(kvh),
-                      int(j * kKeys), int(seq), &bar_v[s]);
+        for (int g = 0; g < kVGroupsPerTile; ++g) {
+          const uint32_t n = j * kVGroupsPerTile + g, s = n % kVSlots;
+          if (n >= kVSlots && !wait_or_abort(&v_empty[s], ((n / kVSlots) - 1) & 1, abort))
+            return false;
+          mbar_arrive_expect_tx(&bar_v[s], kBoxBytes);
+          for (int d = 0; d < kD / 64; ++d)
+            tma_load_4d(smem + Smem::v + s * kBoxBytes + d * (kBoxBytes / 4), &map_v, d * 64,
+                        int(kvh), int(j * kKeys + g * kVKeys), int(seq), &bar_v[s]);
+          v_groups = n + 1;
+        }
         return true;
       };
-      uint32_t k_issued = 0, v_issued = 0;
-      if (n_tiles > 0 && load_k(0))
-        k_issued = 1;
-      for (uint32_t j = 0; k_issued > j && j < n_tiles; ++j) {
-        if (j + 1 < n_tiles) {
-          if (!load_k(j + 1))
-            break;
-          k_issued = j + 2;
-        }
-        if (!load_v(j))
+      // Issue order K_0, then per tile j: K_{j+1}, V_j (K runs a tile ahead).
+      bool fine = n_tiles > 0 && load_k(0);
+      for (uint32_t j = 0; fine && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles && !load_k(j + 1))
           break;
-        v_issued = j + 1;
+        fine = load_v(j);
       }
       // Let every issued copy land before shared memory can be released.
-      for (uint32_t j = k_issued > kKStages ? k_issued - kKStages : 0; j < k_issued; ++j)
-        mbar_wait(&bar_k[j % kKStages], (j / kKStages) & 1);
-      for (uint32_t j = v_issued > kVStages ? v_issued - kVStages : 0; j < v_issued; ++j)
-        mbar_wait(&bar_v[j % kVStages], (j / kVStages) & 1);
+      mbar_wait(q_full, 0);
+      for (uint32_t n = k_boxes > kKSlots ? k_boxes - kKSlots : 0; n < k_boxes; ++n)
+        mbar_wait(&bar_k[n % kKSlots], (n / kKSlots) & 1);
+      for (uint32_t n = v_groups > kVSlots ? v_groups - kVSlots : 0; n < v_groups; ++n)
+        mbar_wait(&bar_v[n % kVSlots], (n / kVSlots) & 1);
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
@@ -221,41 +225,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(kRows, kKeys, false);
       constexpr uint32_t idesc_o = idesc_f16(kRows, kD, true);
+      const uint32_t q_base = smem_u32(smem + Smem::q);
       const uint32_t k_base = smem_u32(smem + Smem::k);
       const uint32_t v_base = smem_u32(smem + Smem::v);
-      bool ok = wait_or_abort(q_ready, 0, abort);
+      bool ok = wait_or_abort(q_full, 0, abort);
       tc_fence_after();
       auto issue_pv = [&](uint32_t i) -> bool {
-        const int sb = i % kSBuffers, sv = i % kVStages;
+        const int sb = i % kSBuffers;
         if (!wait_or_abort(&p_ready[sb], (i / kSBuffers) & 1, abort))
           return false;
-        if (!wait_or_abort(&bar_v[sv], (i / kVStages) & 1, abort))
-          return false;
         tc_fence_after();
-        const uint32_t p_tmem = tmem + kColS + sb * kKeys;  // P over the S buffer
+        const uint32_t p_tmem = tmem + kColS + sb * kKeys;  // P (fp16 pairs) over the S buffer
+        for (int g = 0; g < kVGroupsPerTile; ++g) {
+          const uint32_t n = i * kVGroupsPerTile + g, s = n % kVSlots;
+          if (!wait_or_abort(&bar_v[s], (n / kVSlots) & 1, abort))
+            return false;
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < kKeys / 16; ++ks) {
-          const uint64_t b = smem_desc(v_base + sv * kKVBytes + ks * 2048, kKVBytes / 4, 1024);
-          mma_ts(tmem + kColO, p_tmem + ks * 8, b, idesc_o, (i > 0 || ks > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kVKeys / 16; ++kk) {
+            const int ks = g * (kVKeys / 16) + kk;
+            const uint64_t b = smem_desc(v_base + s * kBoxBytes + kk * 2048, kBoxBytes / 4, 1024);
+            mma_ts(tmem + kColO, p_tmem + ks * 8, b, idesc_o, (i > 0 || ks > 0) ? 1u : 0u);
+          }
+          mma_commit(&v_empty[s]);
         }
-        mma_commit(&v_empty[sv]);
         mma_commit(o_done);
         return true;
       };
       for (uint32_t j = 0; ok && j < n_tiles; ++j) {
-        const int sk = j % kKStages, sb = j % kSBuffers;
-        if (!wait_or_abort(&bar_k[sk], (j / kKStages) & 1, abort)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+        const int sb = j % kSBuffers;
+        for (int b = 0; ok && b < kKBoxesPerTile; ++b) {
+          const uint32_t n = j * kKBoxesPerTile + b, s = n % kKSlots;
+          if (!wait_or_abort(&bar_k[s], (n / kKSlots) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < kD / 16; ++ks) {
-          const uint32_t box = ks >> 2, off = (ks & 3) * 32;
-          const uint64_t kb = smem_desc(k_base + sk * kKVBytes + box * (kKVBytes / 4) + off, 16, 1024);
-          mma_ts(tmem + kColS + sb * kKeys, tmem + kColQ + ks * 8, kb, idesc_s, ks > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t qa = smem_desc(q_base + b * kBoxBytes + kk * 32, 16, 1024);
+            const uint64_t kb = smem_desc(k_base + s * kBoxBytes + kk * 32, 16, 1024);
+            mma_ss(tmem + kColS + sb * kKeys, qa, kb, idesc_s, (b > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&k_empty[s]);
         }
-        mma_commit(&k_empty[sk]);
+        if (!ok)
+          break;
         mma_commit(&s_full[sb]);
         if (j >= 1 && !issue_pv(j - 1))
           ok = false;
@@ -278,32 +293,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool valid = token < a.tokens;
     const uint32_t limit = a.past + min(token, a.tokens - 1);  // last visible key
     const uint32_t first_masked_tile = (a.past + t0) / kKeys;   // tiles before are fully visible
-    constexpr int kHalf = kKeys / 2;
+    constexpr int kHalf = kKeys / 2;                            // keys per warp of the pair
     uint64_t *my_pair = &pair_bar[quarter];
     uint32_t pair_phase = 0;
-
-    // Q -> TMEM: this warp writes dims [128*half, 128*half + 128) of its row
-    // (fp16 pairs, 64 columns); rows past the last token are zero.
-    {
-      const uint4 *src = reinterpret_cast<const uint4 *>(
-          a.q + ((size_t(seq) * a.tokens + token) * a.q_heads + head) * kD + half * (kD / 2));
-#pragma unroll
-      for (int chunk = 0; chunk < 2; ++chunk) {
-        uint32_t r[32];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint4 w = valid ? __ldg(src + chunk * 8 + i) : make_uint4(0u, 0u, 0u, 0u);
-          r[4 * i + 0] = w.x;
-          r[4 * i + 1] = w.y;
-          r[4 * i + 2] = w.z;
-          r[4 * i + 3] = w.w;
-        }
-        tmem_st32(lane_base + kColQ + half * 64 + chunk * 32, r);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(q_ready);
-    }
+    float *row_max = reinterpret_cast<float *>(smem + Smem::row_max);
 
     float m = -INFINITY, l = 0.f;
     bool ok = true;
@@ -316,38 +309,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       uint32_t raw[2][32];
-      tmem_ld32(lane_base + kColS + s * kKeys, raw[0]);
-      tmem_ld32(lane_base + kColS + s * kKeys + 32, raw[1]);
+      const uint32_t s_cols = lane_base + kColS + s * kKeys + half * kHalf;
+      tmem_ld32(s_cols, raw[0]);
+      tmem_ld32(s_cols + 32, raw[1]);
       tmem_wait_ld();
       // Raw scores; the 1/sqrt(D) * log2(e) scale is folded into the
       // exponent's FFMA below (it is positive, so the max commutes with it).
-      float x[kKeys];
+      float x[kHalf];
 #pragma unroll
-      for (int c = 0; c < kKeys; ++c)
+      for (int c = 0; c < kHalf; ++c)
         x[c] = __uint_as_float(raw[c >> 5][c & 31]);
       const bool masked_tile = j >= first_masked_tile;
       if (masked_tile) {
-        const int lim = int(limit) - int(j * kKeys);
+        const int lim = int(limit) - int(j * kKeys + half * kHalf);
 #pragma unroll
-        for (int c = 0; c < kKeys; ++c)
+        for (int c = 0; c < kHalf; ++c)
           if (c > lim)
             x[c] = -INFINITY;
-      }
-      // Both warps of the pair have read S_j before either overwrites it with P.
-      if (!pair_sync(my_pair, (pair_phase++) & 1, abort)) {
-        ok = false;
-        break;
       }
       float mx[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         mx[i] = x[i];
 #pragma unroll
-      for (int c = 8; c < kKeys; ++c)
+      for (int c = 8; c < kHalf; ++c)
         mx[c & 7] = fmaxf(mx[c & 7], x[c]);
-      const float tmax =
-          fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * a.scale_log2;
+      const float pmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      // Exchange the partial maxima (slot by tile parity, so a fast warp
+      // cannot overwrite a value its partner has yet to read).  After the
+      // rendezvous both warps have also read their S columns, so either may
+      // write P over them.
+      float *slot = row_max + (j & 1) * 2 * kRows;
+      slot[half * kRows + row] = pmax;
+      if (!pair_sync(my_pair, (pair_phase++) & 1, abort)) {
+        ok = false;
+        break;
+      }
+      const float tmax = fmaxf(pmax, slot[(1 - half) * kRows + row]) * a.scale_log2;
       const bool need = tmax > m + kRescaleThreshold;
       if (__any_sync(0xffffffffu, need)) {
         const float next = need ? tmax : m;
@@ -374,34 +373,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= alpha;
         m = next;
       }
-      // p = 2^(s*scale - m) for this warp's 32 keys.  With kPolyEvery > 0,
-      // that share of the exponentials of fully visible tiles runs on the FMA
-      // pipe (exp2_fma); tiles with masked (-inf) scores use ex2 throughout.
+      // p = 2^(s*scale - m) for this warp's 64 keys, as fp16 pairs over the
+      // S buffer: keys 64*half.. -> columns 32*half..
       uint32_t packed[kHalf / 2];
       float sums[4] = {0.f, 0.f, 0.f, 0.f};
       const float neg_m = -m, scale = a.scale_log2;
-      // The half is chosen with a compile-time offset so x[] stays in registers.
-      auto exponentiate = [&](auto offset) {
-        constexpr int kOff = decltype(offset)::value;
 #pragma unroll
-        for (int c = 0; c < kHalf; c += 2) {
-          const float a0 = fmaf(x[kOff + c], scale, neg_m);
-          const float a1 = fmaf(x[kOff + c + 1], scale, neg_m);
-          const bool poly =
-              kPolyEvery > 0 && !masked_tile && ((c / 2) % kPolyEvery) == kPolyEvery - 1;
-          const float p0 = fast_exp2(a0);
-          const float p1 = poly ? exp2_fma(a1) : fast_exp2(a1);
-          sums[(c >> 1) & 3] += p0 + p1;
-          packed[c >> 1] = pack_half2(p0, p1);
-        }
-      };
-      if (half == 0)
-        exponentiate(std::integral_constant<int, 0>{});
-      else
-        exponentiate(std::integral_constant<int, kHalf>{});
+      for (int c = 0; c < kHalf; c += 2) {
+        const float p0 = fast_exp2(fmaf(x[c], scale, neg_m));
+        const float p1 = fast_exp2(fmaf(x[c + 1], scale, neg_m));
+        sums[(c >> 1) & 3] += p0 + p1;
+        packed[c >> 1] = pack_half2(p0, p1);
+      }
       l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
-      // P as fp16 pairs over the S buffer: keys 32*half.. -> columns 16*half..
-      tmem_st16(lane_base + kColS + s * kKeys + half * (kHalf / 2), packed);
+      tmem_st32(lane_base + kColS + s * kKeys + half * (kHalf / 2), packed);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_ready[s]);
@@ -439,9 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(kTmemCols)
-                 : "memory");
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 

@@ -279,20 +279,31 @@ int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *
   const uint32_t G = p.queryHeads / p.kvHeads;
   const uint32_t rows = p.past + p.tokens;
   const uint64_t D = kD;
-  CUtensorMap mk, mv;
-  // caches [batch][rows][Hkv][D] at sequence stride cache_stride: box = 64 dims x 1 head x 64 keys.
+  CUtensorMap mq, mk, mv;
+  // caches [batch][rows][Hkv][D] at sequence stride cache_stride: K boxes are
+  // 64 dims x 1 head x 128 keys, V boxes 64 dims x 1 head x 32 keys.
   {
     const uint64_t seq_bytes = batch > 1 ? uint64_t(cache_stride) * 2 : uint64_t(rows) * p.kvHeads * D * 2;
     const uint64_t dims[4] = {D, p.kvHeads, rows, batch};
     const uint64_t strides[3] = {D * 2, uint64_t(p.kvHeads) * D * 2, seq_bytes};
-    const uint32_t box[4] = {64, 1, uint32_t(kKeys), 1};
-    if (int s = encode_map_4d(&mk, k, dims, strides, box))
+    const uint32_t kbox[4] = {64, 1, uint32_t(kKeys), 1};
+    const uint32_t vbox[4] = {64, 1, uint32_t(kVKeys), 1};
+    if (int s = encode_map_4d(&mk, k, dims, strides, kbox))
       return s;
-    if (int s = encode_map_4d(&mv, v, dims, strides, box))
+    if (int s = encode_map_4d(&mv, v, dims, strides, vbox))
+      return s;
+  }
+  // q [batch][tokens][Hq][D]: a box is the CTA's 128 rows (G heads x 128/G
+  // tokens) x 64 dims, rows in (token, head) order.
+  {
+    const uint64_t dims[4] = {D, p.queryHeads, p.tokens, batch};
+    const uint64_t strides[3] = {D * 2, uint64_t(p.queryHeads) * D * 2,
+                                 uint64_t(p.tokens) * p.queryHeads * D * 2};
+    const uint32_t box[4] = {64, G, uint32_t(kRows) / G, 1};
+    if (int s = encode_map_4d(&mq, q, dims, strides, box))
       return s;
   }
   Args a;
-  a.q = reinterpret_cast<const __half *>(q);
   a.out = reinterpret_cast<__half *>(out);
   a.tokens = p.tokens;
   a.q_heads = p.queryHeads;
@@ -305,7 +316,7 @@ int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *
   if (int s = allow_smem(reinterpret_cast<const void *>(gqa_prefill_tcgen05), Smem::alloc, dev))
     return s;
   dim3 grid(a.tiles_per_head, p.kvHeads, batch);
-  gqa_prefill_tcgen05<<<grid, kThreads, Smem::alloc, stream>>>(mk, mv, a);
+  gqa_prefill_tcgen05<<<grid, kThreads, Smem::alloc, stream>>>(mq, mk, mv, a);
   return launched("gqaFlashAttention (tensor cores)");
 }
 
