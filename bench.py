@@ -560,6 +560,11 @@ def run_reference(args, dist):
 
 def main():
     args = parse_args()
+    # Only the JSON line goes to stdout: libraries that print at start-up
+    # (NCCL's version banner, for one) are sent to stderr.
+    result_out = os.fdopen(os.dup(sys.stdout.fileno()), "w")
+    sys.stdout.flush()
+    os.dup2(sys.stderr.fileno(), sys.stdout.fileno())
     dist = Dist(args.gpus)
     try:
         if args.impl == "reference":
@@ -567,7 +572,7 @@ def main():
         else:
             line = run_ours(args, dist)
         if dist.rank == 0 and line is not None:
-            print(json.dumps(line), flush=True)
+            print(json.dumps(line), file=result_out, flush=True)
     finally:
         dist.close()
 

@@ -72,10 +72,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
   return done != 0;
 }
 
+// Non-suspending test of a phase: cheaper than try_wait when the phase has
+// already completed, which matters in a thread that issues tensor-core MMAs
+// (a suspending wait there leaves the MMA queue to run dry).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, unsigned parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Returns false (and
 // raises kErrWaitTimeout) if it has not completed within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
-  if (mbar_try_wait(bar, parity))
+  if (mbar_test_wait(bar, parity))
     return true;
   const uint64_t start = global_timer_ns();
   while (true) {
@@ -94,7 +109,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
 // times out sets that flag, so every role leaves its loop.
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, unsigned parity,
                                               volatile uint32_t *abort) {
-  if (mbar_try_wait(bar, parity))
+  if (mbar_test_wait(bar, parity))
     return true;
   const uint64_t start = global_timer_ns();
   while (true) {

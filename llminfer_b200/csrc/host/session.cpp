@@ -226,6 +226,29 @@ extern "C" int llmi_cuda_session_open(const llmi_stack_config *config, void *str
       return e;
     }
   }
+  // The decode workspace is sized once, for the largest need over every
+  // `past` the session can reach (the split changes every 16 keys), so no
+  // step allocates: steps can be captured into CUDA graphs.
+  if (c.hasGqa()) {
+    std::vector<uint64_t> pasts;
+    for (uint64_t past = 0; past < c.capacity; past += 16)
+      pasts.push_back(past);
+    pasts.push_back(c.capacity - 1);
+    size_t need = 0;
+    for (const uint64_t past : pasts) {
+      llmi_gqa_params g{1, c.queryHeads, c.kvHeads, c.headDim, unsigned(past)};
+      const size_t bytes = llmi_cuda_gqa_decode_workspace(&g, c.batch);
+      if (!bytes) {
+        delete s;
+        return fail(LLMI_CUDA_ERROR, "decode workspace: %s", last_error());
+      }
+      need = std::max(need, bytes);
+    }
+    if (int e = ensure_workspace(*s, need)) {
+      delete s;
+      return e;
+    }
+  }
   if (int e = zero_states(*s)) {
     delete s;
     return e;

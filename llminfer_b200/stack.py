@@ -217,6 +217,8 @@ class StackRun:
         self.dec_free = [torch.cuda.Event() for _ in range(2)]
         for e in self.dec_free:
             e.record(self.comm)
+        self.step_done = torch.cuda.Event()
+        self.graphs = None  # per decode step, once capture_decode() has run
         n = plan.world
         # Without a process group (dist None) a multi-rank plan runs one
         # shard on this GPU and leaves the outputs unshared (emulation).
@@ -270,11 +272,39 @@ class StackRun:
         buf = step & 1
         out = self.dec_out[buf]
         self.stream.wait_event(self.dec_free[buf])
-        self.session.enqueue(1, self._dec_tables[buf])
+        if self.graphs is not None:
+            with torch.cuda.stream(self.stream):
+                self.graphs[step].replay()
+        else:
+            self.session.enqueue(1, self._dec_tables[buf])
         if self.gathering:
-            self.comm.wait_event(self.events[-1])
+            self.step_done.record(self.stream)
+            self.comm.wait_event(self.step_done)
             self._gather(self.dec_gathered, out)
         self.dec_free[buf].record(self.comm)
+
+    def capture_decode(self):
+        """Captures each decode step's launches into its own CUDA graph (the
+        step's `past` is part of its kernel arguments), so a step costs one
+        graph launch on the host instead of ~2 launches per layer.  Call right
+        after a prefill: capturing runs nothing on the GPU but advances the
+        session's `past` through every decode step, so reset the session and
+        run the prefill again before replaying with run_decode_step."""
+        torch = self.torch
+        if self.session.past != self.prefill:
+            raise RuntimeError("capture_decode needs the session right after a prefill")
+        torch.cuda.synchronize()
+        self.session.set_layer_events(None)
+        graphs = []
+        try:
+            for step in range(self.decode):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=self.stream):
+                    self.session.enqueue(1, self._dec_tables[step & 1])
+                graphs.append(g)
+        finally:
+            self.session.set_layer_events(self.events)
+        self.graphs = graphs
 
     def join(self):
         self.stream.wait_stream(self.comm)
@@ -305,6 +335,7 @@ class StackRun:
 
     def close(self):
         self.torch.cuda.synchronize()
+        self.graphs = None
         self.session.set_layer_events(None)
         self.session.close()
 
@@ -334,14 +365,20 @@ def stack_costs(kinds, batch, prefill, decode, shape):
 
 
 def run_stack(torch, dist, world, rank, batch=16, prefill=8192, decode=256, layers=32,
-              shape=None, repeats=1, seed=SEED):
-    """Times `repeats` (prefill, decode) runs; returns rank-0 metrics (max over ranks)."""
+              shape=None, repeats=1, seed=SEED, graphs=True):
+    """Times `repeats` (prefill, decode) runs; returns rank-0 metrics (max over ranks).
+    With `graphs` the decode steps are replayed from CUDA graphs captured
+    before the timed runs."""
     shape = dict(QWEN35_4B if shape is None else shape)
     kinds = qwen35_kinds(layers)
     plan = ShardPlan.make(world, rank, batch, shape)
     run = StackRun(torch, kinds, batch, prefill, decode, shape, plan, dist=dist, seed=seed)
     try:
         run.warmup()
+        if graphs and decode > 0:
+            run.run_prefill()
+            run.capture_decode()
+            run.reset()
         pre_ms, dec_ms, issue_ms = [], [], []
         for _ in range(repeats):
             if dist is not None and world > 1:
@@ -388,6 +425,7 @@ def run_stack(torch, dist, world, rank, batch=16, prefill=8192, decode=256, laye
         # Host time to issue the decode steps (rank 0): near decode_ms means launch-bound.
         "decode_host_issue_ms": round(statistics.median(issue_ms), 3),
         "repeats": repeats,
+        "decode_steps_from": "CUDA graphs captured per step" if graphs else "session enqueue",
         "cost_model": {"prefill_gflop": round(2 * costs["prefill_macs"] / 1e9, 1),
                        "prefill_gqa_gflop": round(2 * costs["prefill_gqa_macs"] / 1e9, 1),
                        "decode_gb": round(costs["decode_bytes"] / 1e9, 2)},

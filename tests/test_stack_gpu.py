@@ -81,3 +81,29 @@ def test_stack_benchmark_runs_and_reports():
     r = S.run_stack(torch, None, 1, 0, batch=2, prefill=96, decode=4, layers=8, shape=SHAPE)
     assert r["prefill_ms"] > 0 and r["decode_ms"] > 0
     assert r["cost_model"]["prefill_gflop"] > 0 and r["decode_tok_s"] > 0
+
+
+def test_decode_steps_replayed_from_cuda_graphs_match_enqueue():
+    plan = S.ShardPlan.make(1, 0, BATCH, SHAPE)
+    run = S.StackRun(torch, KINDS, BATCH, PREFILL, DECODE, SHAPE, plan, dist=None, seed=13)
+    try:
+        def decode_outputs():
+            run.run_prefill()
+            outs = []
+            for s in range(DECODE):
+                run.run_decode_step(s)
+                run.join()
+                torch.cuda.synchronize()
+                outs.append(run.dec_out[s & 1].clone())
+            return torch.stack(outs)
+
+        eager = decode_outputs()
+        run.reset()
+        run.run_prefill()
+        run.capture_decode()
+        run.reset()
+        replayed = decode_outputs()
+        run.session.sync()
+        assert torch.equal(eager, replayed)
+    finally:
+        run.close()
