@@ -159,6 +159,14 @@ int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch,
  * read after each step (MetalExecutor.mm:180-187). */
 int llmi_cuda_poll_error(void *stream);
 
+/* Self-test of the failure path, for tests and health checks: launches on
+ * `stream` one small kernel whose bounded wait on an mbarrier that nothing
+ * completes gives up after limit_us (0 < limit_us <= 1e6) and raises the
+ * device error word, exactly as a kernel's timed-out wait does.  The next
+ * llmi_cuda_poll_error on that stream then returns LLMI_DEVICE_TIMEOUT.
+ * Nothing faults or hangs. */
+int llmi_cuda_selftest_wait_timeout(unsigned limit_us, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Attention-stack session: the CUDA counterpart of MetalSession
  * (include/llminfer/Backend/Metal/MetalSession.h:28-44) reduced to the
@@ -225,6 +233,13 @@ int llmi_cuda_session_sync(llmi_session *session);
  * the following layers compute.  The events are borrowed, not destroyed. */
 int llmi_cuda_session_set_layer_events(llmi_session *session,
                                        void *const *events, unsigned count);
+
+/* Fault injection for tests: the next step or enqueue on this session also
+ * launches llmi_cuda_selftest_wait_timeout(limit_us) after its kernels, so
+ * its completion check reports LLMI_DEVICE_TIMEOUT and the session becomes
+ * invalid, as after a real device-side failure (MetalExecutor.mm:285-287).
+ * limit_us = 0 cancels a pending injection. */
+int llmi_cuda_session_inject_fault(llmi_session *session, unsigned limit_us);
 
 /* MetalSession::reset (MetalExecutor.mm:294-298): zero all states, past = 0,
  * clear the invalid mark. */

@@ -77,12 +77,14 @@ SIGNATURES = [
      [POINTER(DeltaParams), c_uint, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
       c_void_p, c_void_p, c_void_p]),
     ("llmi_cuda_poll_error", c_int, [c_void_p]),
+    ("llmi_cuda_selftest_wait_timeout", c_int, [c_uint, c_void_p]),
     ("llmi_cuda_session_open", c_int, [POINTER(StackConfig), c_void_p, POINTER(c_void_p)]),
     ("llmi_cuda_session_close", None, [c_void_p]),
     ("llmi_cuda_session_step", c_int, [c_void_p, c_uint, POINTER(LayerIO), c_int]),
     ("llmi_cuda_session_enqueue", c_int, [c_void_p, c_uint, POINTER(LayerIO)]),
     ("llmi_cuda_session_sync", c_int, [c_void_p]),
     ("llmi_cuda_session_set_layer_events", c_int, [c_void_p, POINTER(c_void_p), c_uint]),
+    ("llmi_cuda_session_inject_fault", c_int, [c_void_p, c_uint]),
     ("llmi_cuda_session_reset", c_int, [c_void_p]),
     ("llmi_cuda_session_past", c_uint64, [c_void_p]),
     ("llmi_cuda_session_is_invalid", c_int, [c_void_p]),

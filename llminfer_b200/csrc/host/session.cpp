@@ -17,6 +17,8 @@
 #include "attention_graph.h"
 #include "status.h"
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
@@ -39,6 +41,7 @@ struct llmi_session {
   bool invalid = false;
   std::string plan;
   std::vector<cudaEvent_t> layerEvents;  // borrowed; recorded after each layer
+  unsigned injectFaultUs = 0;             // > 0: the next step also runs the wait self-test
 
   ~llmi_session() {
     for (auto *list : {&keys, &values, &recurrent})
@@ -126,6 +129,12 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
     const llmi_layer_io &x = io[op.layer];
     int e = LLMI_OK;
     size_t count = 1;
+    // One NVTX range per op (no-op unless a profiler is attached), named
+    // like its first --plan dispatch.
+    struct Range {
+      explicit Range(const char *name) { nvtxRangePushA(name); }
+      ~Range() { nvtxRangePop(); }
+    } range(next < dispatches.size() ? dispatches[next].kernel : "op");
     switch (op.kind) {
     case OpKind::KvAppend: {
       const unsigned row = c.kvHeads * c.headDim;
@@ -184,6 +193,13 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
         s.plan += line;
       }
     next += count;
+  }
+  if (s.injectFaultUs) {
+    launchedAny = true;
+    const unsigned limit = s.injectFaultUs;
+    s.injectFaultUs = 0;
+    if (int e = llmi_cuda_selftest_wait_timeout(limit, s.stream))
+      return e;
   }
   return LLMI_OK;
 }
@@ -330,6 +346,16 @@ extern "C" int llmi_cuda_session_set_layer_events(llmi_session *s, void *const *
     list[l] = static_cast<cudaEvent_t>(events[l]);
   }
   s->layerEvents = std::move(list);
+  return LLMI_OK;
+}
+
+extern "C" int llmi_cuda_session_inject_fault(llmi_session *s, unsigned limit_us) {
+  clear_error();
+  if (!s)
+    return fail(LLMI_INVALID_ARGUMENT, "inject_fault: null session");
+  if (limit_us > 1000000u)
+    return fail(LLMI_INVALID_ARGUMENT, "inject_fault: limit %u us above 1 s", limit_us);
+  s->injectFaultUs = limit_us;
   return LLMI_OK;
 }
 

@@ -664,6 +664,34 @@ extern "C" int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch
 
 // ---- device error word ---------------------------------------------------------------
 
+namespace {
+// Self-test of the failure path: waits on an mbarrier that nothing ever
+// completes, gives up after `limit_ns` like every bounded wait of the
+// kernels, and raises the error word.  It faults and hangs nothing.
+__global__ void selftest_wait_timeout(unsigned long long limit_ns) {
+  __shared__ uint64_t never;
+  if (threadIdx.x != 0)
+    return;
+  mbar_init(&never, 1);
+  fence_barrier_init();
+  const uint64_t start = global_timer_ns();
+  while (!mbar_try_wait(&never, 0)) {
+    if (global_timer_ns() - start > limit_ns) {
+      raise_error(kErrWaitTimeout);
+      return;
+    }
+  }
+}
+}  // namespace
+
+extern "C" int llmi_cuda_selftest_wait_timeout(unsigned limit_us, void *stream) {
+  clear_error();
+  if (!limit_us || limit_us > 1000000u)
+    return fail(LLMI_INVALID_ARGUMENT, "selftest: limit %u us outside (0, 1 s]", limit_us);
+  selftest_wait_timeout<<<1, 32, 0, as_stream(stream)>>>(uint64_t(limit_us) * 1000u);
+  return launched("selftest_wait_timeout");
+}
+
 extern "C" int llmi_cuda_poll_error(void *stream) {
   clear_error();
   if (int s = check_cuda(cudaStreamSynchronize(as_stream(stream)), "stream synchronize"))

@@ -121,6 +121,11 @@ def poll_error(stream: torch.cuda.Stream | None = None) -> None:
     check(lib.llmi_cuda_poll_error(_stream(stream)))
 
 
+def selftest_wait_timeout(limit_us: int = 1000, stream: torch.cuda.Stream | None = None) -> None:
+    """Launches the bounded-wait self-test; the next poll_error raises LLMI_DEVICE_TIMEOUT."""
+    check(lib.llmi_cuda_selftest_wait_timeout(limit_us, _stream(stream)))
+
+
 @dataclass
 class LayerTensors:
     """One layer's step operands (see LayerIO in llmi_cuda.h)."""
@@ -189,6 +194,11 @@ class AttentionSession:
 
     def reset(self) -> None:
         check(lib.llmi_cuda_session_reset(self._handle))
+
+    def inject_fault(self, limit_us: int = 1000) -> None:
+        """The next step also runs the bounded-wait self-test, so it fails with
+        LLMI_DEVICE_TIMEOUT and the session becomes invalid until reset."""
+        check(lib.llmi_cuda_session_inject_fault(self._handle, limit_us))
 
     def set_layer_events(self, events) -> None:
         """Record events[l] on the session stream after layer l of every step

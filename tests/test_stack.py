@@ -119,3 +119,44 @@ def test_gloo_all_gather_reassembles_layer_output():
     result = mp.Manager().dict()
     mp.spawn(_gather_worker, args=(world, _free_port(), full, result), nprocs=world, join=True)
     assert dict(result) == {0: True, 1: True}
+
+
+def _rank_loss_worker(rank, world, port, result):
+    import datetime
+    import time
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        os._exit(3)  # this rank is lost between steps: no collective of its own in flight
+    plan = S.ShardPlan.make(world, rank, 4, SMALL)
+    mine = torch.ones(4 // plan.seq_groups, 2, 16)
+    gathered = torch.empty(world, *mine.shape)
+    t0 = time.monotonic()
+    try:
+        dist.all_gather_into_tensor(gathered.view(-1, *mine.shape[1:]), mine)
+        result[rank] = ("completed", time.monotonic() - t0)
+    except Exception as exc:  # the survivor must see an error, not wait forever
+        result[rank] = ("error: " + type(exc).__name__, time.monotonic() - t0)
+    os._exit(0)
+
+
+def test_lost_rank_surfaces_as_an_error_not_a_hang():
+    ctx = mp.get_context("spawn")
+    result = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_loss_worker, args=(r, 2, port, result)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung on the collective of a lost peer"
+    assert procs[1].exitcode == 3
+    outcome, seconds = result[0]
+    assert outcome.startswith("error"), outcome
+    assert seconds < 60
