@@ -6,6 +6,8 @@
 // reports launch errors through the status / last-error convention.
 #include "llmi_cuda.h"
 
+#include <cstdlib>
+
 #include "cache_append.cuh"
 #include "common.cuh"
 #include "delta_chunk_tc.cuh"
@@ -13,6 +15,7 @@
 #include "gqa_decode.cuh"
 #include "gqa_flash_simt.cuh"
 #include "gqa_prefill_tc.cuh"
+#include "gqa_prefill_tc2.cuh"
 #include "host/status.h"
 
 #include <cudaTypedefs.h>
@@ -261,6 +264,18 @@ int encode_map_3d(CUtensorMap *map, CUtensorMapDataType type, const void *base,
   return LLMI_OK;
 }
 
+// The tensor-core prefill runs on CTA pairs (cta_group::2 MMAs, half of
+// each K/V tile per CTA): 1.3x the single-CTA kernel's rate at long
+// prompts.  LLMI_PREFILL_CTA_PAIRS=0 selects the single-CTA kernel; the
+// variable is read once per process.
+bool prefill_on_pairs() {
+  static const bool on = [] {
+    const char *e = std::getenv("LLMI_PREFILL_CTA_PAIRS");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // The tensor-core prefill applies to head_dim 256 with a query group that
 // divides the 128-row tile, 16-byte aligned operands and cache strides.
 bool prefill_tc_fits(const llmi_gqa_params &p, unsigned batch, const void *q, const void *k,
@@ -313,6 +328,38 @@ int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *
   a.tok_per_tile = kRows / G;
   a.tiles_per_head = (p.tokens + a.tok_per_tile - 1) / a.tok_per_tile;
   a.scale_log2 = kLog2e / std::sqrt(float(kD));
+  if (prefill_on_pairs()) {
+    // CTA pairs: each CTA stages K boxes of 64 keys x 64 dims and V boxes
+    // of 128 keys x 64 dims.
+    const uint64_t seq_bytes = batch > 1 ? uint64_t(cache_stride) * 2 : uint64_t(rows) * p.kvHeads * D * 2;
+    const uint64_t dims[4] = {D, p.kvHeads, rows, batch};
+    const uint64_t strides[3] = {D * 2, uint64_t(p.kvHeads) * D * 2, seq_bytes};
+    const uint32_t kbox[4] = {64, 1, uint32_t(prefill_tc2::kHalfKeys), 1};
+    const uint32_t vbox[4] = {64, 1, uint32_t(prefill_tc2::kKeys), 1};
+    if (int s = encode_map_4d(&mk, k, dims, strides, kbox))
+      return s;
+    if (int s = encode_map_4d(&mv, v, dims, strides, vbox))
+      return s;
+    a.tiles_per_head += a.tiles_per_head & 1u;
+    auto kernel = prefill_tc2::gqa_prefill_pair;
+    if (int s = allow_smem(reinterpret_cast<const void *>(kernel), prefill_tc2::Smem::alloc, dev))
+      return s;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.tiles_per_head, p.kvHeads, batch);
+    cfg.blockDim = dim3(prefill_tc2::kThreads);
+    cfg.dynamicSmemBytes = prefill_tc2::Smem::alloc;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (int s = check_cuda(cudaLaunchKernelEx(&cfg, kernel, mq, mk, mv, a), "cudaLaunchKernelEx"))
+      return s;
+    return launched("gqaFlashAttention (tensor cores, CTA pairs)");
+  }
   if (int s = allow_smem(reinterpret_cast<const void *>(gqa_prefill_tcgen05), Smem::alloc, dev))
     return s;
   dim3 grid(a.tiles_per_head, p.kvHeads, batch);

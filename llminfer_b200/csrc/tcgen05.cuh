@@ -39,6 +39,13 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
          (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 
+// Advances a shared-memory descriptor's start address by `bytes` (a multiple
+// of 16) with one 32-bit add: the 14-bit address field cannot carry into the
+// next field for shared addresses below 256 KiB.
+__device__ __forceinline__ uint64_t desc_add(uint64_t desc, uint32_t bytes) {
+  return (desc & 0xFFFFFFFF00000000ull) | uint32_t(uint32_t(desc) + (bytes >> 4));
+}
+
 // Instruction descriptor for kind::f16: f16 A/B, f32 accumulator; an operand
 // is K-major unless its *_mn_major flag is set (bits 15 / 16).
 __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool b_mn_major,
@@ -160,6 +167,137 @@ __device__ __forceinline__ void bulk_wait_read() {
 // Waits until this thread's bulk stores have completed.
 __device__ __forceinline__ void bulk_wait() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// ---- CTA pairs (cta_group::2): one thread of the even CTA issues M=256 MMAs
+// whose operands and accumulators are split between the two CTAs' shared and
+// tensor memory.  No load here uses cluster multicast.
+
+// Shared::cluster address of this CTA's variable at `local` in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (this CTA's or
+// the peer's), with the default (CTA-scope) release.  The data these arrivals
+// announce travels on other paths (TMA transaction bytes; tensor-memory stores
+// ordered by tcgen05 fences), and a cluster-scope release would stall the
+// thread until its outstanding bulk copies complete: measured at half speed.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+// Bounded, abort-aware wait (as wait_or_abort) with cluster-scope acquire,
+// for barriers that the peer CTA of a pair arrives on.
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint64_t *bar, unsigned parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, unsigned parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool wait_or_abort_cluster(uint64_t *bar, unsigned parity,
+                                                      volatile uint32_t *abort) {
+  if (mbar_test_wait_cluster(bar, parity))
+    return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait_cluster(bar, parity))
+        return true;
+    if (*abort)
+      return false;
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      raise_error(kErrWaitTimeout);
+      *abort = 1u;
+      return false;
+    }
+  }
+}
+
+// Whole-cluster barrier (every thread of both CTAs).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// TMA tile load into this CTA's shared memory whose completion is counted on
+// the mbarrier at shared::cluster address `bar` (the even CTA's).
+__device__ __forceinline__ void tma_load_4d_pair(void *dst, const CUtensorMap *map, int c0, int c1,
+                                                 int c2, int c3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_ss_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_ts_pair(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on the mbarrier at `bar`'s offset in both CTAs of the pair once
+// every MMA this thread issued so far has retired.
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(uint16_t(3))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t tmem, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols)
+               : "memory");
 }
 
 // Prefetches a box of a tensor into L2 (no shared-memory destination).

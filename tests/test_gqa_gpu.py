@@ -7,6 +7,10 @@ bar max-abs <= 1e-2, rel-L2 <= 2e-3 against the fp64 dense oracle elsewhere.
 Outputs are pre-filled with NaN (as FlashAttentionTest.mm:41 does) so an
 unwritten element fails.
 """
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 import torch
@@ -67,6 +71,7 @@ def test_prefill_known_answers(case):
     (2, 300, 0, 16, 4, 256),   # many key tiles: running-max rescales, stage reuse
     (2, 40, 10, 8, 1, 256),    # group of 8 (16 tokens per tile)
     (2, 50, 3, 4, 4, 256),     # group of 1 (128 tokens per tile)
+    (1, 1100, 200, 16, 4, 256),  # 11 key tiles: K and V rings wrap, odd pair count
     (1, 7, 0, 32, 2, 256),     # group of 16, single partial tile
     (2, 19, 3, 4, 2, 12),      # odd head_dim (CUDA-core path)
     (1, 9, 40, 6, 2, 40),
@@ -139,3 +144,15 @@ def test_poll_error_is_clean_after_work():
     q, k, v = _inputs.gqa_case(2, 1, 64, 16, 4, 256, seed=14)
     ops.gqa_decode(dev(q), dev(k), dev(v), 64)
     ops.poll_error()
+
+
+def test_single_cta_prefill_kernel():
+    """The single-CTA tensor-core prefill (LLMI_PREFILL_CTA_PAIRS=0, read
+    once per process) passes the same prefill parity cases in a child."""
+    env = dict(os.environ, LLMI_PREFILL_CTA_PAIRS="0")
+    here = os.path.dirname(os.path.abspath(__file__))
+    run = subprocess.run(
+        [sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider", "-m", "gpu",
+         "-k", "prefill and not single_cta", os.path.join(here, "test_gqa_gpu.py")],
+        env=env, capture_output=True, text=True, timeout=600)
+    assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-3000:]
