@@ -87,11 +87,14 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, unsigned parity) {
   return done != 0;
 }
 
+// The waits below test the phase inline (one instruction when it has
+// completed) and keep the spin-and-timeout loop out of line: the kernels
+// wait at dozens of places, and inlining every loop bloats their code past
+// what the instruction cache holds.
+
 // Waits for the phase with the given parity to complete.  Returns false (and
 // raises kErrWaitTimeout) if it has not completed within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
-  if (mbar_test_wait(bar, parity))
-    return true;
+__device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, unsigned parity) {
   const uint64_t start = global_timer_ns();
   while (true) {
     for (int i = 0; i < 64; ++i)
@@ -103,14 +106,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
     }
   }
 }
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
+  return mbar_test_wait(bar, parity) || mbar_wait_slow(bar, parity);
+}
 
 // Bounded wait for kernels whose roles depend on one another: it also gives
 // up as soon as another role has set the CTA's abort flag, and a wait that
 // times out sets that flag, so every role leaves its loop.
-__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, unsigned parity,
-                                              volatile uint32_t *abort) {
-  if (mbar_test_wait(bar, parity))
-    return true;
+__device__ __noinline__ bool wait_or_abort_slow(uint64_t *bar, unsigned parity,
+                                                volatile uint32_t *abort) {
   const uint64_t start = global_timer_ns();
   while (true) {
     for (int i = 0; i < 32; ++i)
@@ -124,6 +128,10 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, unsigned parity,
       return false;
     }
   }
+}
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, unsigned parity,
+                                              volatile uint32_t *abort) {
+  return mbar_test_wait(bar, parity) || wait_or_abort_slow(bar, parity, abort);
 }
 
 // ---- cp.async -----------------------------------------------------------------

@@ -166,8 +166,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                const __grid_constant__ CUtensorMap map_v,
                const __grid_constant__ CUtensorMap map_out, const delta::Args a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Rounded up to 1024 bytes by an offset from the shared array itself, so
+  // the compiler keeps every access through `smem` a shared-memory one (a
+  // round trip through an integer address would make them generic).
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gt = tid & (kGroup - 1);  // thread within its group = its TMEM lane
@@ -370,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int hr = warp & 1;
         const int t = 32 * hr + lane;
         const float g_t = gs.g2[t], b_t = arow ? gs.bet[t] : 1.f;
-#pragma unroll
+#pragma unroll 1
         for (int h = 0; h < 2; ++h) {
           const int s0 = 32 * h;
           if (h > hr) {
@@ -591,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (named_sync_or(kBarLocal, kGroup, fail))
         break;
       {
-#pragma unroll
+#pragma unroll 1
         for (int h = 0; h < 2; ++h) {
           uint32_t v[32];
           tmem_ld32(tl + kColW + 32 * h, v);
@@ -727,7 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       {
         const float egl = gs.egl[0];
-#pragma unroll
+#pragma unroll 1
         for (int q4 = 0; q4 < 4; ++q4) {
           uint32_t v[32];
           tmem_ld32(tl + kColS + 32 * q4, v);
@@ -747,7 +749,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       m4_pending = -1;
       tc_fence_after();
-#pragma unroll
+#pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         uint32_t u[32], w[32];
         tmem_ld32(tl + kColU + 32 * h, u);
@@ -800,7 +802,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool q_next = n + 2 < n_chunks;
       if (q_next)
         load_q(n + 2, qr);
-#pragma unroll
+#pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         uint32_t ya[32], yd[32];
         tmem_ld32(tl + kColA + C + 32 * h, ya);
@@ -814,7 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ys[(32 * h + j) * DV] =
               __float2half_rn(fmaf(e[j], __uint_as_float(ya[j]), __uint_as_float(yd[j])));
       }
-#pragma unroll
+#pragma unroll 1
       for (int q4 = 0; q4 < 4; ++q4) {
         uint32_t v[32];
         tmem_ld32(tl + kColS + 32 * q4, v);

@@ -112,8 +112,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, const Args a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Rounded up to 1024 bytes by an offset from the shared array itself, so
+  // the compiler keeps every access through `smem` a shared-memory one (a
+  // round trip through an integer address would make them generic).
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Smem::bars);
   uint64_t *q_full = bars + 0;      // Q landed
   uint64_t *bar_k = bars + 1;       // [kKSlots] K box landed

@@ -223,10 +223,8 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, unsigned pa
       : "memory");
   return done != 0;
 }
-__device__ __forceinline__ bool wait_or_abort_cluster(uint64_t *bar, unsigned parity,
-                                                      volatile uint32_t *abort) {
-  if (mbar_test_wait_cluster(bar, parity))
-    return true;
+__device__ __noinline__ bool wait_or_abort_cluster_slow(uint64_t *bar, unsigned parity,
+                                                        volatile uint32_t *abort) {
   const uint64_t start = global_timer_ns();
   while (true) {
     for (int i = 0; i < 32; ++i)
@@ -240,6 +238,10 @@ __device__ __forceinline__ bool wait_or_abort_cluster(uint64_t *bar, unsigned pa
       return false;
     }
   }
+}
+__device__ __forceinline__ bool wait_or_abort_cluster(uint64_t *bar, unsigned parity,
+                                                      volatile uint32_t *abort) {
+  return mbar_test_wait_cluster(bar, parity) || wait_or_abort_cluster_slow(bar, parity, abort);
 }
 
 // Whole-cluster barrier (every thread of both CTAs).
