@@ -39,13 +39,15 @@
 //
 // One CTA owns one (sequence, value head) and walks its chunks in order, as
 // two warpgroups that run a chunk apart:
-//   warps 0-3  the chunk-local chain of chunk n: k rows (fp32, TMA-staged a
-//              chunk ahead) into the fp16 [K; Q] tile, M1, A and P, the
-//              triangular solve, M2/M3 (under which warp 0 derives the next
-//              chunk's gates), W;
-//   warps 4-7  the state chain of chunk n-1: M4, V', M5/M6, y (through a
-//              shared-memory tile and a TMA store) and the state; then the q
-//              rows of chunk n+1 into the [K; Q] buffer M5/M6 just released.
+//   warps 0-3  the chunk-local chain of chunk n: M1, A and P, the
+//              triangular solve, M2/M3, W;
+//   warps 4-7  the state chain of chunk n-1: M4 (under which warp 4 derives
+//              chunk n+1's gates), V', M5/M6, y (through a shared-memory tile
+//              and a TMA store) and the state; then the k rows (fp32,
+//              TMA-staged a chunk ahead) and q rows of chunk n+1 into the
+//              [K; Q] buffer M5/M6 just released, in fp16.
+// The local chain is the longer one, so the conversions and the gates sit in
+// the state chain, which would otherwise wait for the local one.
 // [K; Q] and P are double-buffered; the groups hand buffers back and forth
 // through mbarriers (MMA commits for "the MMAs reading it are done").  Each
 // group's TMEM lanes are its threads (warp w % 4 owns lanes 32 (w % 4)..);
@@ -188,7 +190,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *bar_xready = bars + 8;  // [2] [K; Q] and P buffers released by M5/M6 and the q
                                     //     rows of the buffer's next chunk written (state -> local)
   uint64_t *bar_du = bars + 10;     // U read from TMEM (state -> local)
-  uint64_t *bar_k = bars + 11;      // k rows staged (local)
+  uint64_t *bar_k = bars + 11;      // k rows staged (state)
+  uint64_t *bar_gates = bars + 12;  // a chunk's gates computed (state -> local)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Smem::tmem_slot);
   volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(smem + Smem::abort_flag);
   float *graw = reinterpret_cast<float *>(smem + Smem::graw);
@@ -214,129 +217,99 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tl = tmem + (uint32_t(32 * (warp & 3)) << 16);  // this warp's TMEM lane quarter
 
+  auto issue_gates = [&](uint32_t chunk) {  // warp 4
+    const uint32_t t0 = chunk * C;
+    const int valid = int(min(uint32_t(C), a.tokens - t0));
+    const size_t tok0 = size_t(seq) * a.tokens + t0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = lane + 32 * i, t = idx & (C - 1);
+      const bool in = t < valid;
+      const float *src =
+          (idx < C ? a.decay : a.beta) + (tok0 + (in ? t : 0)) * a.value_heads + vh;
+      cp_async4(graw + idx, src, in ? 4u : 0u);
+    }
+    cp_async_commit();
+  };
+  // Warp 4: gates of `chunk` from graw (G = inclusive cumsum of log(decay),
+  // beta; pad tokens decay 1, beta 0), everything in log2 units.  A decay
+  // of exactly 0 gets log2 -1e4: every factor 2^(G_t - G_s) across it is 0,
+  // and G keeps full precision in the differences that stay.  (MUFU lg2 /
+  // ex2: their relative error, ~2^-22, is far below the fp16 rounding of
+  // the operands these factors scale.)
+  auto gates = [&](uint32_t chunk) {
+    Gates &gs = gate_sets[chunk % kGateSets];
+    const int valid = int(min(uint32_t(C), a.tokens - chunk * C));
+    cp_async_wait_all();
+    __syncwarp();
+    float la[2], bb[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int t = 2 * lane + i;
+      const bool in = t < valid;
+      const float d = graw[t];
+      la[i] = in ? (d > 0.f ? fast_log2(d) : -1e4f) : 0.f;
+      bb[i] = in ? graw[C + t] : 0.f;
+    }
+    const float pair = la[0] + la[1];
+    float incl = pair;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off)
+        incl += y;
+    }
+    const float gl = __shfl_sync(0xffffffffu, incl, 31);
+    const float g[2] = {incl - pair + la[0], incl};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int t = 2 * lane + i;
+      gs.g2[t] = g[i];
+      gs.eg[t] = fast_exp2(g[i]);
+      gs.ekg[t] = fast_exp2(gl - g[i]);
+      gs.bet[t] = bb[i];
+    }
+    // The block ends: token 16 b + 15 is the second token of lane 8 b + 7.
+    const float ge = __shfl_sync(0xffffffffu, incl, (lane & ~7) | 7);
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+      gs.ev[2 * lane + i] = fast_exp2(ge - g[i]);
+    if (lane == 0)
+      gs.egl[0] = fast_exp2(gl);
+    __syncwarp();
+  };
+  auto issue_k = [&](uint32_t chunk) {
+    mbar_arrive_expect_tx(bar_k, kKBytes);
+    tma_load_3d(smem + Smem::Kst, &map_k, int(kh * DK), int(chunk * C), int(seq), bar_k);
+  };
   if (warp < 4) {
     // ======================= local chain (warps 0-3) =======================
     const bool elected = gt == 0;
     // Parity of a phase issued but not yet seen complete (-1: none); drained
     // on the way out if the loop ends early.
-    int m1_pending = -1, m23_pending = -1, v_pending = -1, k_pending = -1;
+    int m1_pending = -1, m23_pending = -1, v_pending = -1;
     auto issue_v = [&](uint32_t chunk) {
       mbar_arrive_expect_tx(bar_v, kVBytes);
       const int t0 = int(chunk * C);
       tma_load_3d(smem + Smem::Vraw, &map_v, int(vh * DV), t0, int(seq), bar_v);
       tma_load_3d(smem + Smem::Vraw + 8192, &map_v, int(vh * DV + 64), t0, int(seq), bar_v);
     };
-    auto issue_gates = [&](uint32_t chunk) {  // warp 0
-      const uint32_t t0 = chunk * C;
-      const int valid = int(min(uint32_t(C), a.tokens - t0));
-      const size_t tok0 = size_t(seq) * a.tokens + t0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int idx = lane + 32 * i, t = idx & (C - 1);
-        const bool in = t < valid;
-        const float *src =
-            (idx < C ? a.decay : a.beta) + (tok0 + (in ? t : 0)) * a.value_heads + vh;
-        cp_async4(graw + idx, src, in ? 4u : 0u);
-      }
-      cp_async_commit();
-    };
-    // Warp 0: gates of `chunk` from graw (G = inclusive cumsum of log(decay),
-    // beta; pad tokens decay 1, beta 0), everything in log2 units.  A decay
-    // of exactly 0 gets log2 -1e4: every factor 2^(G_t - G_s) across it is 0,
-    // and G keeps full precision in the differences that stay.  (MUFU lg2 /
-    // ex2: their relative error, ~2^-22, is far below the fp16 rounding of
-    // the operands these factors scale.)
-    auto gates = [&](uint32_t chunk) {
-      Gates &gs = gate_sets[chunk % kGateSets];
-      const int valid = int(min(uint32_t(C), a.tokens - chunk * C));
-      cp_async_wait_all();
-      __syncwarp();
-      float la[2], bb[2];
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int t = 2 * lane + i;
-        const bool in = t < valid;
-        const float d = graw[t];
-        la[i] = in ? (d > 0.f ? fast_log2(d) : -1e4f) : 0.f;
-        bb[i] = in ? graw[C + t] : 0.f;
-      }
-      const float pair = la[0] + la[1];
-      float incl = pair;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off)
-          incl += y;
-      }
-      const float gl = __shfl_sync(0xffffffffu, incl, 31);
-      const float g[2] = {incl - pair + la[0], incl};
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int t = 2 * lane + i;
-        gs.g2[t] = g[i];
-        gs.eg[t] = fast_exp2(g[i]);
-        gs.ekg[t] = fast_exp2(gl - g[i]);
-        gs.bet[t] = bb[i];
-      }
-      // The block ends: token 16 b + 15 is the second token of lane 8 b + 7.
-      const float ge = __shfl_sync(0xffffffffu, incl, (lane & ~7) | 7);
-#pragma unroll
-      for (int i = 0; i < 2; ++i)
-        gs.ev[2 * lane + i] = fast_exp2(ge - g[i]);
-      if (lane == 0)
-        gs.egl[0] = fast_exp2(gl);
-      __syncwarp();
-    };
-    auto issue_k = [&](uint32_t chunk) {
-      mbar_arrive_expect_tx(bar_k, kKBytes);
-      tma_load_3d(smem + Smem::Kst, &map_k, int(kh * DK), int(chunk * C), int(seq), bar_k);
-    };
     if (elected) {
       issue_v(0);
       v_pending = 0;
-      issue_k(0);
-      k_pending = 0;
-    }
-    if (warp == 0) {
-      issue_gates(0);
-      gates(0);
-      if (n_chunks > 1)
-        issue_gates(1);
     }
 
     for (uint32_t n = 0; n < n_chunks; ++n) {
       const int b = n & 1;
       Gates &gs = gate_sets[n % kGateSets];
-      uint8_t *X = smem + Smem::X + b * 32768;
       const uint32_t xs = sbase + Smem::X + b * 32768;
       const bool more = n + 1 < n_chunks;
 
-      // L1. [K; Q] buffer b is released (and holds chunk n's q rows) and the
-      //     k rows are staged: k into the buffer's rows 0-63 (fp16), then
-      //     the next chunk's k rows into the staging tile.
+      // L1. [K; Q] buffer b holds chunk n's k and q rows (fp16, written by
+      //     the state group once M5/M6 of chunk n - 2 released it).
       bool fail = !wait_or_abort(&bar_xready[b], (n >> 1) & 1, abort);
-      if (elected && !fail) {
-        fail = !wait_or_abort(bar_k, n & 1, abort);
-        if (!fail)
-          k_pending = -1;
-      }
       if (named_sync_or(kBarLocal, kGroup, fail))
         break;
-      {
-        const float *kr = reinterpret_cast<const float *>(smem + Smem::Kst);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int idx = gt + kGroup * i, t = idx >> 4, ch = idx & 15;
-          const float4 *k4 = reinterpret_cast<const float4 *>(kr + t * DK + 8 * ch);
-          st16(X + (ch >> 3) * 16384 + sw128_chunk(t, ch & 7), pack8(k4[0], k4[1]));
-        }
-      }
-      fence_proxy_async();
-      named_sync(kBarLocal, kGroup);
-      if (elected && more) {
-        issue_k(n + 1);
-        k_pending = int((n + 1) & 1);
-      }
 
       // L2. M1: D1 = [K; Q] K^T.
       if (elected) {
@@ -350,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(bar_m1);
         m1_pending = int(n & 1);
       }
-      fail = !wait_or_abort(bar_m1, n & 1, abort);
+      fail = !wait_or_abort(bar_m1, n & 1, abort) || !wait_or_abort(bar_gates, n & 1, abort);
       if (named_sync_or(kBarLocal, kGroup, fail))
         break;
       m1_pending = -1;
@@ -569,11 +542,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (named_sync_or(kBarLocal, kGroup, fail))
         break;
-      if (warp == 0 && more) {
-        gates(n + 1);
-        if (n + 2 < n_chunks)
-          issue_gates(n + 2);
-      }
       fail = !wait_or_abort(bar_m23, n & 1, abort);
       if (named_sync_or(kBarLocal, kGroup, fail))
         break;
@@ -617,16 +585,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(bar_m23, unsigned(m23_pending));
       if (v_pending >= 0)
         mbar_wait(bar_v, unsigned(v_pending));
-      if (k_pending >= 0)
-        mbar_wait(bar_k, unsigned(k_pending));
     }
-    if (warp == 0)
-      cp_async_wait_all();
   } else {
     // ======================= state chain (warps 4-7) =======================
     const bool elected = gt == 0;
     const int dv = gt;  // this thread's value column (TMEM lane)
-    int m4_pending = -1, m56_pending = -1;
+    int m4_pending = -1, m56_pending = -1, k_pending = -1;
+    // Staged k rows of `chunk` (fp32) into rows 0-63 of its [K; Q] buffer
+    // (fp16); every thread must have seen bar_k complete.
+    auto convert_k = [&](uint32_t chunk) {
+      uint8_t *Xb = smem + Smem::X + (chunk & 1) * 32768;
+      const float *kr = reinterpret_cast<const float *>(smem + Smem::Kst);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int idx = gt + kGroup * i, t = idx >> 4, ch = idx & 15;
+        const float4 *k4 = reinterpret_cast<const float4 *>(kr + t * DK + 8 * ch);
+        st16(Xb + (ch >> 3) * 16384 + sw128_chunk(t, ch & 7), pack8(k4[0], k4[1]));
+      }
+      fence_proxy_async();
+    };
     // q rows of `chunk` (fp32, global) into rows 64-127 of its [K; Q] buffer:
     // the loads, then the fp16 stores.
     auto load_q = [&](uint32_t chunk, float4 (&qr)[8][2]) {
@@ -655,8 +632,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async();
     };
-    if (elected && n_chunks > 2)
-      tma_prefetch_3d(&map_q, int(kh * DK), 2 * C, int(seq));
+    if (elected) {
+      issue_k(0);
+      k_pending = 0;
+      if (n_chunks > 2)
+        tma_prefetch_3d(&map_q, int(kh * DK), 2 * C, int(seq));
+    }
+    if (warp == 4) {
+      issue_gates(0);
+      gates(0);
+      if (n_chunks > 1)
+        issue_gates(1);
+      if (lane == 0)
+        mbar_arrive(bar_gates);
+    }
     // Initial state: S^T into TMEM, in fp32 (the accumulator) and fp16 (M4's
     // A operand); the q rows of chunks 0 and 1.
 #pragma unroll
@@ -677,19 +666,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         h[j] = pack_half2(v[2 * j], v[2 * j + 1]);
       tmem_st16(tl + kColST + 16 * q4, h);
     }
-    {
+    // The [K; Q] buffers of chunks 0 and 1 (a failed wait leaves them
+    // unwritten: the local group then fails its own first wait).
+    bool pro_fail = false;
+    for (uint32_t c = 0; c < 2 && c < n_chunks; ++c) {
       float4 qr[8][2];
-      load_q(0, qr);
-      store_q(0, qr);
-      if (n_chunks > 1) {
-        load_q(1, qr);
-        store_q(1, qr);
+      load_q(c, qr);
+      bool f = false;
+      if (elected) {
+        f = !wait_or_abort(bar_k, c & 1, abort);
+        if (!f)
+          k_pending = -1;
+      }
+      if (named_sync_or(kBarState, kGroup, f)) {
+        pro_fail = true;
+        break;
+      }
+      convert_k(c);
+      store_q(c, qr);
+      named_sync(kBarState, kGroup);
+      if (elected && c + 1 < n_chunks) {
+        issue_k(c + 1);
+        k_pending = int((c + 1) & 1);
       }
     }
     tmem_wait_st();
     tc_fence_before();
     named_sync(kBarState, kGroup);
-    if (elected) {
+    if (elected && !pro_fail) {
       mbar_arrive(&bar_xready[0]);
       if (n_chunks > 1)
         mbar_arrive(&bar_xready[1]);
@@ -726,6 +730,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (n + 2 < n_chunks)  // q rows converted at the end of this chunk
           tma_prefetch_3d(&map_q, int(kh * DK), int(t0 + 2 * C), int(seq));
         bulk_wait_read();  // the previous output tile (Ys = Vp) has been read
+      }
+      // The next chunk's gates, needed by the local group from its step L3.
+      if (warp == 4 && n + 1 < n_chunks) {
+        gates(n + 1);
+        if (n + 2 < n_chunks)
+          issue_gates(n + 2);
+        if (lane == 0)
+          mbar_arrive(bar_gates);
       }
       {
         const float egl = gs.egl[0];
@@ -836,16 +848,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       fence_proxy_async();
       tc_fence_before();
-      named_sync(kBarState, kGroup);
+      fail = false;
+      if (elected && q_next) {  // k rows of chunk n + 2 staged
+        fail = !wait_or_abort(bar_k, n & 1, abort);
+        if (!fail)
+          k_pending = -1;
+      }
+      if (named_sync_or(kBarState, kGroup, fail))
+        break;
       if (elected) {
         tma_store_3d(&map_out, smem + Smem::Ys, int(vh * DV), int(t0), int(seq));
         bulk_commit();
       }
       if (q_next) {
+        // Chunk n + 2's k and q rows into the buffer M5/M6 released; then
+        // the staging tile takes the k rows of chunk n + 3.
+        convert_k(n + 2);
         store_q(n + 2, qr);
         named_sync(kBarState, kGroup);
-        if (elected)
+        if (elected) {
+          if (n + 3 < n_chunks) {
+            issue_k(n + 3);
+            k_pending = int((n + 3) & 1);
+          }
           mbar_arrive(&bar_xready[b]);
+        }
       }
     }
     if (elected) {
@@ -853,8 +880,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(bar_m4, unsigned(m4_pending));
       if (m56_pending >= 0)
         mbar_wait(bar_m56, unsigned(m56_pending));
+      if (k_pending >= 0)
+        mbar_wait(bar_k, unsigned(k_pending));
       bulk_wait();
     }
+    if (warp == 4)
+      cp_async_wait_all();
   }
 
   tc_fence_before();
