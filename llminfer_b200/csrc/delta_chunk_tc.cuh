@@ -109,7 +109,7 @@ struct Smem {
   static constexpr int graw = Tu + 8192;           // fp32 decay[64], beta[64] (cp.async)
   static constexpr int gates = graw + 2 * C * 4;   // Gates[kGateSets], by chunk mod kGateSets
   static constexpr int bars = gates + kGateSets * int(sizeof(Gates));
-  static constexpr int kBars = 13;
+  static constexpr int kBars = 14;
   static constexpr int tmem_slot = bars + kBars * 8;
   static constexpr int abort_flag = tmem_slot + 4;
   static constexpr int total = abort_flag + 12;
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     //     rows of the buffer's next chunk written (state -> local)
   uint64_t *bar_du = bars + 10;     // U read from TMEM (state -> local)
   uint64_t *bar_k = bars + 11;      // k rows staged (state)
-  uint64_t *bar_gates = bars + 12;  // a chunk's gates computed (state -> local)
+  uint64_t *bar_gates = bars + 12;  // [2] gates of the chunks of each parity (state -> local)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Smem::tmem_slot);
   volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(smem + Smem::abort_flag);
   float *graw = reinterpret_cast<float *>(smem + Smem::graw);
@@ -317,13 +317,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t id = idesc_f16(128, C, false);
 #pragma unroll
         for (int k = 0; k < DK / 16; ++k) {
-          const uint64_t d = smem_desc(xs + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024);
+          const uint64_t d = desc_add(smem_desc(xs, 16, 1024), (k >> 2) * 16384 + (k & 3) * 32);
           mma_ss(tmem + kColD1, d, d, id, k > 0 ? 1u : 0u);
         }
         mma_commit(bar_m1);
         m1_pending = int(n & 1);
       }
-      fail = !wait_or_abort(bar_m1, n & 1, abort) || !wait_or_abort(bar_gates, n & 1, abort);
+      fail = !wait_or_abort(bar_m1, n & 1, abort) ||
+             !wait_or_abort(&bar_gates[n & 1], (n >> 1) & 1, abort);
       if (named_sync_or(kBarLocal, kGroup, fail))
         break;
       m1_pending = -1;
@@ -531,10 +532,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           constexpr uint32_t id = idesc_f16(128, C, false, true);
 #pragma unroll
           for (int k = 0; k < C / 16; ++k) {
-            mma_ss(tmem + kColW, smem_desc(xs + k * 2048, 16384, 1024),
-                   smem_desc(sbase + Smem::Tw + k * 32, 16, 1024), id, k > 0 ? 1u : 0u);
-            mma_ss(tmem + kColU, smem_desc(sbase + Smem::Vraw + k * 2048, 8192, 1024),
-                   smem_desc(sbase + Smem::Tu + k * 32, 16, 1024), id, k > 0 ? 1u : 0u);
+            mma_ss(tmem + kColW, desc_add(smem_desc(xs, 16384, 1024), k * 2048),
+                   desc_add(smem_desc(sbase + Smem::Tw, 16, 1024), k * 32), id, k > 0 ? 1u : 0u);
+            mma_ss(tmem + kColU, desc_add(smem_desc(sbase + Smem::Vraw, 8192, 1024), k * 2048),
+                   desc_add(smem_desc(sbase + Smem::Tu, 16, 1024), k * 32), id, k > 0 ? 1u : 0u);
           }
           mma_commit(bar_m23);
           m23_pending = int(n & 1);
@@ -638,16 +639,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (n_chunks > 2)
         tma_prefetch_3d(&map_q, int(kh * DK), 2 * C, int(seq));
     }
+    // Gates run two chunks ahead of the local chain: chunks 0 and 1 here,
+    // chunk n + 2 while the state chain works on chunk n.
     if (warp == 4) {
-      issue_gates(0);
-      gates(0);
-      if (n_chunks > 1)
-        issue_gates(1);
-      if (lane == 0)
-        mbar_arrive(bar_gates);
+      for (uint32_t c = 0; c < 2 && c < n_chunks; ++c) {
+        issue_gates(c);
+        gates(c);
+        if (lane == 0)
+          mbar_arrive(&bar_gates[c]);
+      }
+      if (n_chunks > 2)
+        issue_gates(2);
     }
-    // Initial state: S^T into TMEM, in fp32 (the accumulator) and fp16 (M4's
-    // A operand); the q rows of chunks 0 and 1.
+    named_sync(kBarState, kGroup);  // gates of chunk 0 visible to the group
+    // Initial state: S^T into TMEM, in fp16 (M4's A operand) and in fp32 (the
+    // accumulator M6 adds to), the latter already scaled by chunk 0's
+    // e^{G_C}; the q rows of chunks 0 and 1.
+    const float egl0 = gate_sets[0].egl[0];
 #pragma unroll
     for (int q4 = 0; q4 < 4; ++q4) {
       const int key0 = 32 * q4;
@@ -658,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t st[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        st[j] = __float_as_uint(v[j]);
+        st[j] = __float_as_uint(v[j] * egl0);
       tmem_st32(tl + kColS + key0, st);
       uint32_t h[16];
 #pragma unroll
@@ -707,7 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t xs = sbase + Smem::X + b * 32768;
 
       // S1. Chunk n's W, [K; Q], P and U are ready: M4 = S^T [W; Q]^T.
-      //     Meanwhile the state in TMEM is scaled by e^{G_C} for M6.
+      //     (The fp32 state in TMEM is already scaled by e^{G_C} for M6.)
       bool fail = !wait_or_abort(&bar_ready[b], (n >> 1) & 1, abort);
       if (named_sync_or(kBarState, kGroup, fail))
         break;
@@ -718,10 +726,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < DK / 16; ++k) {
           const uint32_t as = tmem + kColST + k * 8;  // 16 keys = 8 columns of fp16 pairs
-          mma_ts(tmem + kColA, as, smem_desc(sbase + Smem::WB + k * 2048, 16384, 1024), id_w,
+          mma_ts(tmem + kColA, as, desc_add(smem_desc(sbase + Smem::WB, 16384, 1024), k * 2048), id_w,
                  k > 0 ? 1u : 0u);
           mma_ts(tmem + kColA + C, as,
-                 smem_desc(xs + (k >> 2) * 16384 + 8192 + (k & 3) * 32, 16, 1024), id_q,
+                 desc_add(smem_desc(xs, 16, 1024), (k >> 2) * 16384 + 8192 + (k & 3) * 32), id_q,
                  k > 0 ? 1u : 0u);
         }
         mma_commit(bar_m4);
@@ -731,27 +739,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_prefetch_3d(&map_q, int(kh * DK), int(t0 + 2 * C), int(seq));
         bulk_wait_read();  // the previous output tile (Ys = Vp) has been read
       }
-      // The next chunk's gates, needed by the local group from its step L3.
-      if (warp == 4 && n + 1 < n_chunks) {
-        gates(n + 1);
-        if (n + 2 < n_chunks)
-          issue_gates(n + 2);
+      // Gates of chunk n + 2, which the local group needs from its step L3.
+      if (warp == 4 && n + 2 < n_chunks) {
+        gates(n + 2);
+        if (n + 3 < n_chunks)
+          issue_gates(n + 3);
         if (lane == 0)
-          mbar_arrive(bar_gates);
-      }
-      {
-        const float egl = gs.egl[0];
-#pragma unroll 1
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint32_t v[32];
-          tmem_ld32(tl + kColS + 32 * q4, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            v[j] = __float_as_uint(__uint_as_float(v[j]) * egl);
-          tmem_st32(tl + kColS + 32 * q4, v);
-        }
-        tmem_wait_st();
+          mbar_arrive(&bar_gates[n & 1]);
       }
 
       // S2. V'^T = U^T - (W S)^T (row = value column, 64 tokens) into Vp,
@@ -792,10 +786,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t id6 = idesc_f16(128, 128, true);
 #pragma unroll
         for (int k = 0; k < C / 16; ++k) {
-          mma_ss(tmem + kColY, smem_desc(sbase + Smem::Vp + k * 32, 16, 1024),
-                 smem_desc(sbase + Smem::P + b * 8192 + k * 32, 16, 1024), id5, k > 0 ? 1u : 0u);
-          mma_ss(tmem + kColS, smem_desc(sbase + Smem::Vg + k * 32, 16, 1024),
-                 smem_desc(xs + k * 2048, 16384, 1024), id6, 1u);
+          mma_ss(tmem + kColY, desc_add(smem_desc(sbase + Smem::Vp, 16, 1024), k * 32),
+                 desc_add(smem_desc(sbase + Smem::P + b * 8192, 16, 1024), k * 32), id5, k > 0 ? 1u : 0u);
+          mma_ss(tmem + kColS, desc_add(smem_desc(sbase + Smem::Vg, 16, 1024), k * 32),
+                 desc_add(smem_desc(xs, 16384, 1024), k * 2048), id6, 1u);
         }
         mma_commit(bar_m56);
         m56_pending = int(n & 1);
@@ -828,6 +822,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           ys[(32 * h + j) * DV] =
               __float2half_rn(fmaf(e[j], __uint_as_float(ya[j]), __uint_as_float(yd[j])));
       }
+      // The state after chunk n: fp16 for the next chunk's M4, and the fp32
+      // accumulator scaled by the next chunk's e^{G_C} for its M6.
+      const float egl_next = last ? 1.f : gate_sets[(n + 1) % kGateSets].egl[0];
 #pragma unroll 1
       for (int q4 = 0; q4 < 4; ++q4) {
         uint32_t v[32];
@@ -839,6 +836,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 16; ++j)
             h[j] = pack_half2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
           tmem_st16(tl + kColST + 16 * q4, h);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = __float_as_uint(__uint_as_float(v[j]) * egl_next);
+          tmem_st32(tl + kColS + 32 * q4, v);
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
