@@ -152,6 +152,104 @@ int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch,
                            const float *beta, const float *decay, float *state,
                            uint16_t *out, void *stream);
 
+/* ---- Producers of the path's operands -------------------------------------
+ * The ops that turn the projections' outputs into the inputs of cacheAppend /
+ * gqaFlashAttention and graphDeltaUpdate (Qwen35ModelBuilder.cpp:146-160 and
+ * :187-192).  fp16 rounding points are the reference's, op by op; row sums
+ * are warp trees, so fp32 results can differ from its serial order in the
+ * last bits.  Argument errors are reported before any launch. */
+
+/* RopeParams (lib/Backend/Metal/Kernels/ReferenceParams.h:44-47). */
+typedef struct {
+  unsigned tokens, heads, headDim, rotaryDim, headStride, past, outputStart;
+  float epsilon, theta;
+} llmi_rope_params;
+
+/* ConvParams (lib/Backend/Metal/Kernels/ReferenceParams.h:32-34). */
+typedef struct {
+  unsigned tokens, channels, kernelSize, applySilu;
+} llmi_conv_params;
+
+/* L2Params (lib/Backend/Metal/Kernels/GraphParams.h:30-33). */
+typedef struct {
+  unsigned rows, width;
+  float epsilon, scale;
+} llmi_l2_params;
+
+/* RowParams (lib/Backend/Metal/Kernels/ReferenceParams.h:23-26). */
+typedef struct {
+  unsigned rows, width;
+  float epsilon;
+} llmi_row_params;
+
+/* DeltaParams (lib/Backend/Metal/Kernels/ReferenceParams.h:40-42), with the
+ * conv kernel size and the L2Norm epsilon of the block. */
+typedef struct {
+  unsigned tokens, keyHeads, keyDim, valueHeads, valueDim, qkvWidth;
+  unsigned kernelSize;
+  float epsilon;
+} llmi_delta_prep_params;
+
+/* q/k RmsNorm + PartialRoPE, fused as normRope
+ * (lib/Backend/Metal/Kernels/Reference.metal:271-293; = rmsNorm :105-117
+ * then partialRope Graph.metal:111-129).  Per sequence s < batch, row r of
+ * tokens*heads reads input + s*input_stride + r*headStride (headDim fp16;
+ * headStride = 2*headDim for q sliced from q_proj's [q|gate] rows) and
+ * writes output + s*output_stride + (outputStart*heads + r)*headDim: for
+ * keys, pass the key cache and outputStart = past (the step's cacheAppend).
+ * x = half(x * rsqrt(mean(x^2) + epsilon) * (1 + weight)), then pairs
+ * (i, i + rotaryDim/2) rotate by (past + token) / theta^(2i/rotaryDim) with
+ * fp16-rounded cos/sin.  headDim <= 1024, rotaryDim even and <= headDim. */
+int llmi_cuda_norm_rope(const llmi_rope_params *p, unsigned batch, const uint16_t *input,
+                        size_t input_stride, const float *weight, uint16_t *output,
+                        size_t output_stride, void *stream);
+
+/* PartialRoPE alone (lib/Backend/Metal/Kernels/Graph.metal:111-129, lowered
+ * at MetalExecutionPlan.cpp:624-634): llmi_cuda_norm_rope without the norm;
+ * epsilon is unused. */
+int llmi_cuda_partial_rope(const llmi_rope_params *p, unsigned batch, const uint16_t *input,
+                           size_t input_stride, uint16_t *output, size_t output_stride,
+                           void *stream);
+
+/* CausalConv1d (causalConv, lib/Backend/Metal/Kernels/Reference.metal:137-158,
+ * lowered at MetalExecutionPlan.cpp:636-647 with applySilu 0).  Per
+ * sequence: input/output [tokens][channels] fp16, weight [channels]
+ * [kernelSize] fp16 (shared), history [channels][kernelSize-1] fp16 (the
+ * ConvHistory state, read then advanced by the step).
+ * out = half(sum_j w[j] x(t-K+1+j)), x before the step from the history;
+ * with applySilu, half(silu(out)). */
+int llmi_cuda_causal_conv(const llmi_conv_params *p, unsigned batch, const uint16_t *input,
+                          size_t input_stride, const uint16_t *weight, uint16_t *history,
+                          size_t history_stride, uint16_t *output, size_t output_stride,
+                          void *stream);
+
+/* L2Norm (l2NormF32, lib/Backend/Metal/Kernels/Graph.metal:96-109):
+ * rows x width fp16 in, fp32 out, x * rsqrt(sum x^2 + epsilon) * scale. */
+int llmi_cuda_l2_norm(const llmi_l2_params *p, const uint16_t *input, float *output,
+                      void *stream);
+
+/* DeltaGates (lib/Backend/Metal/Kernels/Graph.metal:131-144): a, b
+ * [rows][width] fp16, aLog and dtBias [width] fp32 ->
+ * beta = half(sigmoid(b)) and decay = exp(-exp(aLog) softplus(a + dtBias)),
+ * [rows][width] fp32.  epsilon is unused. */
+int llmi_cuda_delta_gates(const llmi_row_params *p, const uint16_t *a, const uint16_t *b,
+                          const float *aLog, const float *dtBias, float *beta, float *decay,
+                          void *stream);
+
+/* The DeltaNet block's operands from its qkv projection, fused: CausalConv1d
+ * with SiLU, the q/k/v Slices and the q and k L2Norms
+ * (Qwen35ModelBuilder.cpp:146-157: q scaled by 1/sqrt(keyDim)).  Per
+ * sequence: qkv [tokens][qkvWidth] fp16 in (qkvWidth = 2*keyHeads*keyDim +
+ * valueHeads*valueDim), conv weight [qkvWidth][kernelSize] fp16, history as
+ * for llmi_cuda_causal_conv; out q and k [tokens][keyHeads*keyDim] fp32 and
+ * v [tokens][valueHeads*valueDim] fp16, the layouts llmi_cuda_delta_update
+ * reads, packed over the batch.  keyDim, valueDim <= 256. */
+int llmi_cuda_delta_prepare(const llmi_delta_prep_params *p, unsigned batch,
+                            const uint16_t *qkv, size_t qkv_stride,
+                            const uint16_t *conv_weight, uint16_t *history,
+                            size_t history_stride, float *q, float *k, uint16_t *v,
+                            void *stream);
+
 /* Synchronises `stream`, then reads and clears the device error word that
  * kernels set when a bounded wait gives up.  Returns LLMI_OK,
  * LLMI_DEVICE_TIMEOUT or LLMI_CUDA_ERROR (for an asynchronous launch or

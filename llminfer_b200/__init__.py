@@ -5,19 +5,22 @@ The product is the C-ABI library llminfer_b200/_lib/libllmi_cuda.so
 against the KV cache, cacheAppend) and the Gated-DeltaNet update (recurrent
 step and chunked prefill), plus the attention-stack session that owns the
 KV caches and recurrent states and lowers each step's ops with the
-reference's --plan kernel names.  This package binds it for Python callers;
-importing it without the built library fails (there is no fallback).
+reference's --plan kernel names.  This package binds it for Python callers.
+The bindings load on first use, and fail loudly without the built library
+(there is no fallback); the build module itself (`python -m
+llminfer_b200.build`) needs no library.
 """
-from ._abi import LlmiError, describe_step, make_stack_config  # noqa: F401
-from . import _abi as abi  # noqa: F401
+import importlib
 
 __all__ = ["abi", "LlmiError", "describe_step", "make_stack_config", "ops"]
 
 
 def __getattr__(name):
-    # torch is imported lazily so host-only users (plan description) do not
-    # pay for it.
+    # The library and torch load lazily: host-only users (plan description)
+    # do not pay for torch, and the build runs with a stale or missing library.
+    if name in ("abi", "LlmiError", "describe_step", "make_stack_config"):
+        abi = importlib.import_module("._abi", __name__)
+        return abi if name == "abi" else getattr(abi, name)
     if name == "ops":
-        import importlib
         return importlib.import_module(".ops", __name__)
     raise AttributeError(name)

@@ -7,7 +7,8 @@ ImportError: there is no fallback implementation of any op.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_char_p, c_int, c_size_t, c_ubyte, c_uint, c_uint16, c_uint64, c_void_p
+from ctypes import (POINTER, c_char_p, c_float, c_int, c_size_t, c_ubyte, c_uint, c_uint16, c_uint64,
+                    c_void_p)
 from pathlib import Path
 
 LIBRARY_PATH = Path(__file__).resolve().parent / "_lib" / "libllmi_cuda.so"
@@ -46,6 +47,34 @@ class DeltaParams(ctypes.Structure):
                 ("valueHeads", c_uint), ("valueDim", c_uint)]
 
 
+class RopeParams(ctypes.Structure):
+    """RopeParams of lib/Backend/Metal/Kernels/ReferenceParams.h:44-47."""
+    _fields_ = [(n, c_uint) for n in ("tokens", "heads", "headDim", "rotaryDim", "headStride",
+                                      "past", "outputStart")] + \
+               [("epsilon", c_float), ("theta", c_float)]
+
+
+class ConvParams(ctypes.Structure):
+    """ConvParams of lib/Backend/Metal/Kernels/ReferenceParams.h:32-34."""
+    _fields_ = [(n, c_uint) for n in ("tokens", "channels", "kernelSize", "applySilu")]
+
+
+class L2Params(ctypes.Structure):
+    """L2Params of lib/Backend/Metal/Kernels/GraphParams.h:30-33."""
+    _fields_ = [("rows", c_uint), ("width", c_uint), ("epsilon", c_float), ("scale", c_float)]
+
+
+class RowParams(ctypes.Structure):
+    """RowParams of lib/Backend/Metal/Kernels/ReferenceParams.h:23-26."""
+    _fields_ = [("rows", c_uint), ("width", c_uint), ("epsilon", c_float)]
+
+
+class DeltaPrepParams(ctypes.Structure):
+    """DeltaParams of ReferenceParams.h:40-42 plus the conv size and L2 epsilon."""
+    _fields_ = [(n, c_uint) for n in ("tokens", "keyHeads", "keyDim", "valueHeads", "valueDim",
+                                      "qkvWidth", "kernelSize")] + [("epsilon", c_float)]
+
+
 class StackConfig(ctypes.Structure):
     _fields_ = [("layers", c_uint), ("layer_kinds", POINTER(c_ubyte)),
                 ("batch", c_uint), ("capacity", c_uint),
@@ -76,6 +105,19 @@ SIGNATURES = [
     ("llmi_cuda_delta_update", c_int,
      [POINTER(DeltaParams), c_uint, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
       c_void_p, c_void_p, c_void_p]),
+    ("llmi_cuda_norm_rope", c_int,
+     [POINTER(RopeParams), c_uint, c_void_p, c_size_t, c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("llmi_cuda_partial_rope", c_int,
+     [POINTER(RopeParams), c_uint, c_void_p, c_size_t, c_void_p, c_size_t, c_void_p]),
+    ("llmi_cuda_causal_conv", c_int,
+     [POINTER(ConvParams), c_uint, c_void_p, c_size_t, c_void_p, c_void_p, c_size_t, c_void_p,
+      c_size_t, c_void_p]),
+    ("llmi_cuda_l2_norm", c_int, [POINTER(L2Params), c_void_p, c_void_p, c_void_p]),
+    ("llmi_cuda_delta_gates", c_int,
+     [POINTER(RowParams), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    ("llmi_cuda_delta_prepare", c_int,
+     [POINTER(DeltaPrepParams), c_uint, c_void_p, c_size_t, c_void_p, c_void_p, c_size_t,
+      c_void_p, c_void_p, c_void_p, c_void_p]),
     ("llmi_cuda_poll_error", c_int, [c_void_p]),
     ("llmi_cuda_selftest_wait_timeout", c_int, [c_uint, c_void_p]),
     ("llmi_cuda_session_open", c_int, [POINTER(StackConfig), c_void_p, POINTER(c_void_p)]),

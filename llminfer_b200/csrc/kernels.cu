@@ -16,6 +16,7 @@
 #include "gqa_flash_simt.cuh"
 #include "gqa_prefill_tc.cuh"
 #include "gqa_prefill_tc2.cuh"
+#include "producers.cuh"
 #include "host/status.h"
 
 #include <cudaTypedefs.h>
@@ -737,6 +738,196 @@ extern "C" int llmi_cuda_selftest_wait_timeout(unsigned limit_us, void *stream) 
     return fail(LLMI_INVALID_ARGUMENT, "selftest: limit %u us outside (0, 1 s]", limit_us);
   selftest_wait_timeout<<<1, 32, 0, as_stream(stream)>>>(uint64_t(limit_us) * 1000u);
   return launched("selftest_wait_timeout");
+}
+
+// ---- producers of the path's operands ---------------------------------------------
+
+namespace {
+
+unsigned grid_for(uint64_t work, unsigned per_block) {
+  const uint64_t blocks = (work + per_block - 1) / per_block;
+  return unsigned(blocks < 0x7fffffffull ? blocks : 0x7fffffffull);
+}
+
+int rope_common(const char *op, const llmi_rope_params *p, unsigned batch, const uint16_t *input,
+                size_t input_stride, const float *weight, uint16_t *output, size_t output_stride,
+                void *stream) {
+  if (!p || !input || !output)
+    return fail(LLMI_INVALID_ARGUMENT, "%s: null parameter or tensor pointer", op);
+  if (!batch || !p->tokens || !p->heads || !p->headDim)
+    return fail(LLMI_INVALID_ARGUMENT, "%s: sizes must be positive", op);
+  if (p->headDim > unsigned(producers::kRopeMaxDim) || p->rotaryDim % 2 ||
+      p->rotaryDim > p->headDim || p->headStride < p->headDim)
+    return fail(LLMI_UNSUPPORTED, "%s: headDim %u, rotaryDim %u, headStride %u", op, p->headDim,
+                p->rotaryDim, p->headStride);
+  const uint64_t rows = uint64_t(p->tokens) * p->heads;
+  if (batch > 1 && (input_stride < rows * p->headStride ||
+                    output_stride < (uint64_t(p->outputStart) * p->heads + rows) * p->headDim))
+    return fail(LLMI_INVALID_ARGUMENT, "%s: sequence strides overlap", op);
+  producers::RopeArgs a;
+  a.input = reinterpret_cast<const __half *>(input);
+  a.input_stride = input_stride;
+  a.weight = weight;
+  a.output = reinterpret_cast<__half *>(output);
+  a.output_stride = output_stride;
+  a.batch = batch;
+  a.tokens = p->tokens;
+  a.heads = p->heads;
+  a.head_dim = p->headDim;
+  a.rotary_dim = p->rotaryDim;
+  a.head_stride = p->headStride;
+  a.past = p->past;
+  a.output_start = p->outputStart;
+  a.epsilon = p->epsilon;
+  a.theta = p->theta;
+  const bool vec = p->headDim % 8 == 0 && p->headStride % 8 == 0 && aligned16(input) &&
+                   aligned16(output) && input_stride % 8 == 0 && output_stride % 8 == 0;
+  const unsigned grid = grid_for(rows * batch, producers::kRopeWarps);
+  cudaStream_t s = as_stream(stream);
+  if (vec)
+    producers::norm_rope<true><<<grid, 32 * producers::kRopeWarps, 0, s>>>(a);
+  else
+    producers::norm_rope<false><<<grid, 32 * producers::kRopeWarps, 0, s>>>(a);
+  return launched(op);
+}
+
+int conv_args(const char *op, const llmi_conv_params *p, unsigned batch, const uint16_t *input,
+              size_t input_stride, const uint16_t *weight, uint16_t *history,
+              size_t history_stride, producers::ConvArgs &a) {
+  if (!p || !input || !weight || (!history && p->kernelSize > 1))
+    return fail(LLMI_INVALID_ARGUMENT, "%s: null parameter or tensor pointer", op);
+  if (!batch || !p->tokens || !p->channels || !p->kernelSize)
+    return fail(LLMI_INVALID_ARGUMENT, "%s: sizes must be positive", op);
+  const uint64_t hist = uint64_t(p->channels) * (p->kernelSize - 1);
+  if (batch > 1 && (input_stride < uint64_t(p->tokens) * p->channels || history_stride < hist))
+    return fail(LLMI_INVALID_ARGUMENT, "%s: sequence strides overlap", op);
+  a.input = reinterpret_cast<const __half *>(input);
+  a.input_stride = input_stride;
+  a.weight = reinterpret_cast<const __half *>(weight);
+  a.history = reinterpret_cast<const __half *>(history);
+  a.history_stride = history_stride;
+  a.batch = batch;
+  a.tokens = p->tokens;
+  a.channels = p->channels;
+  a.kernel = p->kernelSize;
+  a.apply_silu = p->applySilu != 0;
+  return LLMI_OK;
+}
+
+// Runs after the step's outputs (stream order), which read the old history.
+int advance_history(const producers::ConvArgs &a, uint16_t *history, cudaStream_t s) {
+  if (a.kernel < 2)
+    return LLMI_OK;
+  const uint64_t n = uint64_t(a.batch) * a.channels;
+  producers::conv_history<<<grid_for(n, 256), 256, 0, s>>>(a, reinterpret_cast<__half *>(history));
+  return launched("causalConv (history)");
+}
+
+}  // namespace
+
+extern "C" int llmi_cuda_norm_rope(const llmi_rope_params *p, unsigned batch,
+                                   const uint16_t *input, size_t input_stride, const float *weight,
+                                   uint16_t *output, size_t output_stride, void *stream) {
+  clear_error();
+  if (!weight)
+    return fail(LLMI_INVALID_ARGUMENT, "normRope: null weight");
+  return rope_common("normRope", p, batch, input, input_stride, weight, output, output_stride,
+                     stream);
+}
+
+extern "C" int llmi_cuda_partial_rope(const llmi_rope_params *p, unsigned batch,
+                                      const uint16_t *input, size_t input_stride,
+                                      uint16_t *output, size_t output_stride, void *stream) {
+  clear_error();
+  return rope_common("partialRope", p, batch, input, input_stride, nullptr, output,
+                     output_stride, stream);
+}
+
+extern "C" int llmi_cuda_causal_conv(const llmi_conv_params *p, unsigned batch,
+                                     const uint16_t *input, size_t input_stride,
+                                     const uint16_t *weight, uint16_t *history,
+                                     size_t history_stride, uint16_t *output,
+                                     size_t output_stride, void *stream) {
+  clear_error();
+  producers::ConvArgs a;
+  if (int e = conv_args("causalConv", p, batch, input, input_stride, weight, history,
+                        history_stride, a))
+    return e;
+  if (!output)
+    return fail(LLMI_INVALID_ARGUMENT, "causalConv: null output");
+  if (batch > 1 && output_stride < uint64_t(p->tokens) * p->channels)
+    return fail(LLMI_INVALID_ARGUMENT, "causalConv: sequence strides overlap");
+  cudaStream_t s = as_stream(stream);
+  const uint64_t n = uint64_t(batch) * p->tokens * p->channels;
+  producers::causal_conv<<<grid_for(n, 256), 256, 0, s>>>(a, reinterpret_cast<__half *>(output),
+                                                          output_stride);
+  if (int e = launched("causalConv"))
+    return e;
+  return advance_history(a, history, s);
+}
+
+extern "C" int llmi_cuda_l2_norm(const llmi_l2_params *p, const uint16_t *input, float *output,
+                                 void *stream) {
+  clear_error();
+  if (!p || !input || !output)
+    return fail(LLMI_INVALID_ARGUMENT, "l2NormF32: null parameter or tensor pointer");
+  if (!p->rows || !p->width)
+    return fail(LLMI_INVALID_ARGUMENT, "l2NormF32: sizes must be positive");
+  producers::l2_norm<<<grid_for(p->rows, 8), 256, 0, as_stream(stream)>>>(
+      reinterpret_cast<const __half *>(input), output, p->rows, p->width, p->epsilon, p->scale);
+  return launched("l2NormF32");
+}
+
+extern "C" int llmi_cuda_delta_gates(const llmi_row_params *p, const uint16_t *a,
+                                     const uint16_t *b, const float *aLog, const float *dtBias,
+                                     float *beta, float *decay, void *stream) {
+  clear_error();
+  if (!p || !a || !b || !aLog || !dtBias || !beta || !decay)
+    return fail(LLMI_INVALID_ARGUMENT, "deltaGates: null parameter or tensor pointer");
+  if (!p->rows || !p->width)
+    return fail(LLMI_INVALID_ARGUMENT, "deltaGates: sizes must be positive");
+  const uint64_t n = uint64_t(p->rows) * p->width;
+  producers::delta_gates<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(
+      reinterpret_cast<const __half *>(a), reinterpret_cast<const __half *>(b), aLog, dtBias,
+      beta, decay, n, p->width);
+  return launched("deltaGates");
+}
+
+extern "C" int llmi_cuda_delta_prepare(const llmi_delta_prep_params *p, unsigned batch,
+                                       const uint16_t *qkv, size_t qkv_stride,
+                                       const uint16_t *conv_weight, uint16_t *history,
+                                       size_t history_stride, float *q, float *k, uint16_t *v,
+                                       void *stream) {
+  clear_error();
+  if (!p || !q || !k || !v)
+    return fail(LLMI_INVALID_ARGUMENT, "deltaPrepare: null parameter or tensor pointer");
+  if (!p->keyHeads || !p->keyDim || !p->valueHeads || !p->valueDim)
+    return fail(LLMI_INVALID_ARGUMENT, "deltaPrepare: sizes must be positive");
+  if (p->qkvWidth != 2 * p->keyHeads * p->keyDim + p->valueHeads * p->valueDim)
+    return fail(LLMI_INVALID_ARGUMENT, "deltaPrepare: qkvWidth %u is not 2*%u*%u + %u*%u",
+                p->qkvWidth, p->keyHeads, p->keyDim, p->valueHeads, p->valueDim);
+  if (p->keyDim > 256 || p->valueDim > 256)
+    return fail(LLMI_UNSUPPORTED, "deltaPrepare: keyDim %u / valueDim %u above 256", p->keyDim,
+                p->valueDim);
+  const llmi_conv_params cp{p->tokens, p->qkvWidth, p->kernelSize, 1};
+  producers::PrepArgs a;
+  if (int e = conv_args("deltaPrepare", &cp, batch, qkv, qkv_stride, conv_weight, history,
+                        history_stride, a.conv))
+    return e;
+  a.key_heads = p->keyHeads;
+  a.key_dim = p->keyDim;
+  a.value_heads = p->valueHeads;
+  a.value_dim = p->valueDim;
+  a.epsilon = p->epsilon;
+  a.q = q;
+  a.k = k;
+  a.v = reinterpret_cast<__half *>(v);
+  cudaStream_t s = as_stream(stream);
+  const uint64_t rows = uint64_t(batch) * p->tokens * (2 * p->keyHeads + p->valueHeads);
+  producers::delta_prepare<<<grid_for(rows, 8), 256, 0, s>>>(a);
+  if (int e = launched("deltaPrepare"))
+    return e;
+  return advance_history(a.conv, history, s);
 }
 
 extern "C" int llmi_cuda_poll_error(void *stream) {

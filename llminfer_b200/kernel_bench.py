@@ -11,6 +11,8 @@ on the CPU before timing).  Prints one JSON object.
   python -m llminfer_b200.kernel_bench prefill --batch 1 --tokens 128
   python -m llminfer_b200.kernel_bench delta   --batch 256 --tokens 1 --state-std 0.02
   python -m llminfer_b200.kernel_bench append  --batch 64 --tokens 1 --past 4096
+  python -m llminfer_b200.kernel_bench rope    --batch 16 --tokens 8192 --past 0
+  python -m llminfer_b200.kernel_bench deltaprep --batch 16 --tokens 8192
 """
 from __future__ import annotations
 
@@ -168,9 +170,90 @@ def bench_append(args):
                 gbs=nbytes / (med * 1e-3) / 1e9, check=check)
 
 
+def bench_rope(args):
+    """q and k of a GQA layer: normRope of q (sliced from [q | gate] rows) and
+    of k (written into the key cache at row past)."""
+    gen = torch.Generator(device="cuda").manual_seed(args.seed)
+    B, T, (Hq, Hkv), D = args.batch, args.tokens, args.heads, args.dim
+    rot = D // 4
+    cap = max(args.capacity, args.past + T)
+    qg = torch.randn(B, T, Hq, 2 * D, generator=gen, device="cuda").half()
+    k = torch.randn(B, T, Hkv, D, generator=gen, device="cuda").half()
+    wq = (0.1 * torch.randn(D, generator=gen, device="cuda")).float()
+    wk = (0.1 * torch.randn(D, generator=gen, device="cuda")).float()
+    qo = torch.empty(B, T, Hq, D, dtype=torch.float16, device="cuda")
+    cache = torch.zeros(B, cap, Hkv, D, dtype=torch.float16, device="cuda")
+
+    def fn():
+        ops.norm_rope(qg, wq, args.past, rot, 1e7, head_dim=D, out=qo)
+        ops.norm_rope(k, wk, args.past, rot, 1e7, out=cache, output_start=args.past)
+
+    check = None
+    if not args.no_check:
+        fn()
+        # fp32 RmsNorm (1 + w) and rotate-half RoPE, no intermediate rounding.
+        x = qg[..., :D].float()
+        x = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * (1 + wq)
+        pos = torch.arange(args.past, args.past + T, device="cuda").float()
+        inv = 1.0 / (1e7 ** (torch.arange(0, rot, 2, device="cuda").float() / rot))
+        ang = pos[:, None] * inv[None, :]
+        c, s_ = ang.cos()[None, :, None, :], ang.sin()[None, :, None, :]
+        x1, x2 = x[..., :rot // 2], x[..., rot // 2:rot]
+        ref = torch.cat((x1 * c - x2 * s_, x2 * c + x1 * s_, x[..., rot:]), -1)
+        m, r = errors(qo.float(), ref)
+        check = dict(max_abs=m, rel_l2=r)
+    best, med = time_fn(fn, args.samples, args.warmup)
+    nbytes = (B * T * Hq * D * 2) * 2 + (B * T * Hkv * D * 2) * 2
+    hbm, _, src = peaks()
+    gbs = nbytes / (med * 1e-3) / 1e9
+    return dict(op="normRope (q and k)", batch=B, tokens=T, heads=[Hq, Hkv], dim=D,
+                rotary_dim=rot, best_ms=best, median_ms=med, gbs=gbs, hbm_frac=gbs / hbm,
+                peaks=src, check=check)
+
+
+def bench_deltaprep(args):
+    """The DeltaNet block's q, k, v from its qkv projection (conv + SiLU +
+    L2 norms) and its gates."""
+    gen = torch.Generator(device="cuda").manual_seed(args.seed)
+    B, T = args.batch, args.tokens
+    (Hk, Hv), (dk, dv) = args.delta_heads, args.delta_dims
+    W, K = 2 * Hk * dk + Hv * dv, 4
+    qkv = torch.randn(B, T, W, generator=gen, device="cuda").half()
+    wconv = (0.5 * torch.randn(W, K, generator=gen, device="cuda")).half()
+    hist = torch.zeros(B, W, K - 1, dtype=torch.float16, device="cuda")
+    a = torch.randn(B, T, Hv, generator=gen, device="cuda").half()
+    b = torch.randn(B, T, Hv, generator=gen, device="cuda").half()
+    a_log = torch.randn(Hv, generator=gen, device="cuda").float()
+    dt_bias = torch.randn(Hv, generator=gen, device="cuda").float()
+
+    def fn():
+        ops.delta_prepare(qkv, wconv, hist, Hk, dk, Hv, dv)
+        ops.delta_gates(a, b, a_log, dt_bias)
+
+    check = None
+    if not args.no_check:
+        h0 = torch.zeros_like(hist)
+        q, _, _ = ops.delta_prepare(qkv, wconv, h0, Hk, dk, Hv, dv)
+        # fp32 depthwise conv + SiLU (no intermediate fp16 rounding), q L2 norm.
+        x = torch.cat([torch.zeros_like(hist).float().transpose(1, 2), qkv.float()], 1)
+        conv = sum(x[:, j:j + T] * wconv[:, j].float() for j in range(K))
+        y = conv * torch.sigmoid(conv)
+        qr = y[..., :Hk * dk].reshape(B, T, Hk, dk)
+        qr = (qr * torch.rsqrt(qr.pow(2).sum(-1, keepdim=True) + 1e-6) / math.sqrt(dk))
+        m, r = errors(q, qr.reshape(B, T, -1))
+        check = dict(q_max_abs=m, q_rel_l2=r)
+    best, med = time_fn(fn, args.samples, args.warmup)
+    nbytes = B * T * (W * 2 + 2 * Hk * dk * 4 + Hv * dv * 2 + Hv * 2 * 2 + Hv * 2 * 4)
+    hbm, _, src = peaks()
+    gbs = nbytes / (med * 1e-3) / 1e9
+    return dict(op="deltaPrepare + deltaGates", batch=B, tokens=T, heads=[Hk, Hv],
+                dims=[dk, dv], best_ms=best, median_ms=med, gbs=gbs, hbm_frac=gbs / hbm,
+                peaks=src, check=check)
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("op", choices=["decode", "prefill", "delta", "append"])
+    p.add_argument("op", choices=["decode", "prefill", "delta", "append", "rope", "deltaprep"])
     p.add_argument("--batch", type=int, default=64)
     p.add_argument("--tokens", type=int, default=128)
     p.add_argument("--past", type=int, default=4096)
@@ -192,6 +275,10 @@ def main(argv=None):
         res = bench_gqa(args, decode=False)
     elif args.op == "delta":
         res = bench_delta(args)
+    elif args.op == "rope":
+        res = bench_rope(args)
+    elif args.op == "deltaprep":
+        res = bench_deltaprep(args)
     else:
         res = bench_append(args)
     ops.poll_error()

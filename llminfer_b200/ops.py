@@ -117,6 +117,99 @@ def delta_update(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.
     return out
 
 
+# ---- producers of the path's operands --------------------------------------------
+
+
+def norm_rope(x: torch.Tensor, weight: torch.Tensor | None, past: int, rotary_dim: int,
+              theta: float, eps: float = 1e-6, head_dim: int | None = None,
+              out: torch.Tensor | None = None, output_start: int = 0,
+              stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """normRope (weight given) or partialRope (weight None) over x [B, T, H, W]
+    fp16, whose rows are the first head_dim of each W-wide head.  Writes
+    rows output_start.. of `out` [B, rows, H, head_dim] (a key cache, with
+    output_start = past) or a new [B, T, H, head_dim] tensor."""
+    _need(x, torch.float16, "x")
+    B, T, H, W = x.shape
+    head_dim = head_dim or W
+    if out is None:
+        out = torch.empty(B, T, H, head_dim, dtype=torch.float16, device=x.device)
+    _need(out, torch.float16, "out")
+    p = abi.RopeParams(T, H, head_dim, rotary_dim, W, past, output_start, eps, theta)
+    if weight is None:
+        check(lib.llmi_cuda_partial_rope(ctypes.byref(p), B, x.data_ptr(), x[0].numel(),
+                                         out.data_ptr(), out[0].numel(), _stream(stream)))
+    else:
+        _need(weight, torch.float32, "weight")
+        check(lib.llmi_cuda_norm_rope(ctypes.byref(p), B, x.data_ptr(), x[0].numel(),
+                                      weight.data_ptr(), out.data_ptr(), out[0].numel(),
+                                      _stream(stream)))
+    return out
+
+
+def causal_conv(x: torch.Tensor, weight: torch.Tensor, history: torch.Tensor,
+                apply_silu: bool = False, out: torch.Tensor | None = None,
+                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """causalConv over x [B, T, C] fp16 with weight [C, K] and history
+    [B, C, K-1] (advanced in place)."""
+    for t, n in ((x, "x"), (weight, "weight"), (history, "history")):
+        _need(t, torch.float16, n)
+    B, T, C = x.shape
+    out = torch.empty_like(x) if out is None else out
+    p = abi.ConvParams(T, C, weight.shape[1], 1 if apply_silu else 0)
+    check(lib.llmi_cuda_causal_conv(ctypes.byref(p), B, x.data_ptr(), x[0].numel(),
+                                    weight.data_ptr(), history.data_ptr(), history[0].numel(),
+                                    out.data_ptr(), out[0].numel(), _stream(stream)))
+    return out
+
+
+def l2_norm(x: torch.Tensor, width: int, scale: float, eps: float = 1e-6,
+            stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """l2NormF32: fp16 rows of `width` -> fp32."""
+    _need(x, torch.float16, "x")
+    out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    p = abi.L2Params(x.numel() // width, width, eps, scale)
+    check(lib.llmi_cuda_l2_norm(ctypes.byref(p), x.data_ptr(), out.data_ptr(), _stream(stream)))
+    return out
+
+
+def delta_gates(a: torch.Tensor, b: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor,
+                stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """deltaGates: a, b [..., H] fp16 -> (beta, decay) fp32."""
+    _need(a, torch.float16, "a")
+    _need(b, torch.float16, "b")
+    _need(a_log, torch.float32, "a_log")
+    _need(dt_bias, torch.float32, "dt_bias")
+    heads = a.shape[-1]
+    beta = torch.empty(a.shape, dtype=torch.float32, device=a.device)
+    decay = torch.empty_like(beta)
+    p = abi.RowParams(a.numel() // heads, heads, 0.0)
+    check(lib.llmi_cuda_delta_gates(ctypes.byref(p), a.data_ptr(), b.data_ptr(),
+                                    a_log.data_ptr(), dt_bias.data_ptr(), beta.data_ptr(),
+                                    decay.data_ptr(), _stream(stream)))
+    return beta, decay
+
+
+def delta_prepare(qkv: torch.Tensor, conv_weight: torch.Tensor, history: torch.Tensor,
+                  key_heads: int, key_dim: int, value_heads: int, value_dim: int,
+                  eps: float = 1e-6, stream: torch.cuda.Stream | None = None):
+    """The DeltaNet block's (q, k, v) from its qkv projection [B, T, W] fp16:
+    conv + SiLU, Slices, q/k L2Norm.  Advances history [B, W, K-1] in place."""
+    for t, n in ((qkv, "qkv"), (conv_weight, "conv_weight"), (history, "history")):
+        _need(t, torch.float16, n)
+    B, T, W = qkv.shape
+    kw, vw = key_heads * key_dim, value_heads * value_dim
+    q = torch.empty(B, T, kw, dtype=torch.float32, device=qkv.device)
+    k = torch.empty_like(q)
+    v = torch.empty(B, T, vw, dtype=torch.float16, device=qkv.device)
+    p = abi.DeltaPrepParams(T, key_heads, key_dim, value_heads, value_dim, W,
+                            conv_weight.shape[1], eps)
+    check(lib.llmi_cuda_delta_prepare(ctypes.byref(p), B, qkv.data_ptr(), qkv[0].numel(),
+                                      conv_weight.data_ptr(), history.data_ptr(),
+                                      history[0].numel(), q.data_ptr(), k.data_ptr(),
+                                      v.data_ptr(), _stream(stream)))
+    return q, k, v
+
+
 def poll_error(stream: torch.cuda.Stream | None = None) -> None:
     check(lib.llmi_cuda_poll_error(_stream(stream)))
 

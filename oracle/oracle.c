@@ -280,6 +280,74 @@ void oracle_delta_gates(const float *a, const float *b, const float *aLog,
     }
 }
 
+/* ---- q/k norm and RoPE; causal conv ------------------------------------------- */
+
+void oracle_norm_rope(const oracle_rope_params *p, unsigned batch, const uint16_t *input,
+                      size_t input_stride, const float *weight, uint16_t *output,
+                      size_t output_stride) {
+  const unsigned D = p->headDim, half_r = p->rotaryDim / 2;
+  float *x = (float *)malloc(sizeof(float) * D);
+  for (unsigned s = 0; s < batch; ++s)
+    for (unsigned r = 0; r < p->tokens * p->heads; ++r) {
+      const uint16_t *in = input + s * input_stride + (size_t)r * p->headStride;
+      uint16_t *out = output + s * output_stride + ((size_t)p->outputStart * p->heads + r) * D;
+      if (weight) {
+        float sum = 0.0f;
+        for (unsigned i = 0; i < D; ++i) {
+          const float v = oracle_f16_to_f32(in[i]);
+          sum = fmaf(v, v, sum);
+        }
+        const float scale = 1.0f / sqrtf(sum / (float)D + p->epsilon);
+        for (unsigned i = 0; i < D; ++i)
+          x[i] = round_half(oracle_f16_to_f32(in[i]) * scale * (1.0f + weight[i]));
+      } else {
+        for (unsigned i = 0; i < D; ++i)
+          x[i] = oracle_f16_to_f32(in[i]);
+      }
+      const float position = (float)(p->past + r / p->heads);
+      for (unsigned i = 0; i < half_r; ++i) {
+        const unsigned j = i + half_r;
+        const float phase = position / powf(p->theta, 2.0f * (float)i / (float)p->rotaryDim);
+        const float c = round_half(cosf(phase)), sn = round_half(sinf(phase));
+        const float xv = x[i], yv = x[j];
+        x[i] = round_half(round_half(xv * c) - round_half(yv * sn));
+        x[j] = round_half(round_half(yv * c) + round_half(xv * sn));
+      }
+      for (unsigned i = 0; i < D; ++i)
+        out[i] = oracle_f32_to_f16(x[i]);
+    }
+  free(x);
+}
+
+static float silu_ref(float x) { return x * (1.0f / (1.0f + expf(-x))); }
+
+void oracle_causal_conv(const oracle_conv_params *p, unsigned batch, const uint16_t *input,
+                        size_t input_stride, const uint16_t *weight, uint16_t *history,
+                        size_t history_stride, uint16_t *output, size_t output_stride) {
+  const unsigned H = p->kernelSize - 1;
+  for (unsigned s = 0; s < batch; ++s)
+    for (unsigned c = 0; c < p->channels; ++c) {
+      uint16_t *recent = history + s * history_stride + (size_t)c * H;
+      const uint16_t *filter = weight + (size_t)c * p->kernelSize;
+      for (unsigned t = 0; t < p->tokens; ++t) {
+        const size_t i = (size_t)t * p->channels + c;
+        const uint16_t current = input[s * input_stride + i];
+        float acc = oracle_f16_to_f32(current) * oracle_f16_to_f32(filter[H]);
+        for (unsigned j = 0; j < H; ++j)
+          acc = fmaf(oracle_f16_to_f32(recent[j]), oracle_f16_to_f32(filter[j]), acc);
+        float y = round_half(acc);
+        if (p->applySilu)
+          y = round_half(silu_ref(y));
+        output[s * output_stride + i] = oracle_f32_to_f16(y);
+        if (H) {
+          for (unsigned j = 1; j < H; ++j)
+            recent[j - 1] = recent[j];
+          recent[H - 1] = current;
+        }
+      }
+    }
+}
+
 /* ---- cost model ------------------------------------------------------------- */
 
 uint64_t oracle_gqa_pairs(uint64_t tokens, uint64_t past) {

@@ -103,6 +103,37 @@ void oracle_delta_gates(const float *a, const float *b, const float *aLog,
                         const float *dtBias, size_t rows, unsigned heads,
                         float *beta, float *decay);
 
+/* RopeParams (ReferenceParams.h:44-47) and ConvParams (ReferenceParams.h:32-34). */
+typedef struct {
+  unsigned tokens, heads, headDim, rotaryDim, headStride, past, outputStart;
+  float epsilon, theta;
+} oracle_rope_params;
+typedef struct {
+  unsigned tokens, channels, kernelSize, applySilu;
+} oracle_conv_params;
+
+/* q/k RmsNorm + PartialRoPE, restating rmsNorm (Reference.metal:98-117:
+ * x * rsqrt(sum x^2 / width + eps) * (1 + w), rounded to fp16), rotatePair
+ * (Reference.metal:261-269: phase = position / theta^(2i/R), cos and sin
+ * rounded to fp16, each product rounded to fp16) and the row addressing of
+ * normRope (Reference.metal:271-293).  weight == NULL skips the norm: that
+ * is partialRope (Graph.metal:111-129).  Per sequence s < batch, row r reads
+ * input + s*input_stride + r*headStride and writes output + s*output_stride
+ * + (outputStart*heads + r)*headDim. */
+void oracle_norm_rope(const oracle_rope_params *p, unsigned batch, const uint16_t *input,
+                      size_t input_stride, const float *weight, uint16_t *output,
+                      size_t output_stride);
+
+/* causalConv (Reference.metal:137-158), walked token by token per channel
+ * as the reference does, the history shifting after each token; with
+ * applySilu the output is half(silu(half(acc))), which is also causalConv
+ * (applySilu 0) followed by siluF16 (Graph.metal:70-76).  input/output
+ * [tokens][channels] and history [channels][kernelSize-1] per sequence;
+ * weight [channels][kernelSize]; the history is updated in place. */
+void oracle_causal_conv(const oracle_conv_params *p, unsigned batch, const uint16_t *input,
+                        size_t input_stride, const uint16_t *weight, uint16_t *history,
+                        size_t history_stride, uint16_t *output, size_t output_stride);
+
 /* Logical work of one op, following the reference cost model
  * (lib/GraphIR/Cost.cpp:85-93 traffic, :180-201 math). */
 uint64_t oracle_gqa_pairs(uint64_t tokens, uint64_t past);

@@ -28,6 +28,16 @@ class DeltaParams(ctypes.Structure):
                 ("valueHeads", c_uint), ("valueDim", c_uint)]
 
 
+class RopeParams(ctypes.Structure):
+    _fields_ = [(n, c_uint) for n in ("tokens", "heads", "headDim", "rotaryDim", "headStride",
+                                      "past", "outputStart")] + \
+               [("epsilon", c_float), ("theta", c_float)]
+
+
+class ConvParams(ctypes.Structure):
+    _fields_ = [(n, c_uint) for n in ("tokens", "channels", "kernelSize", "applySilu")]
+
+
 def _ptr(a: np.ndarray, ctype):
     assert a.flags["C_CONTIGUOUS"]
     return a.ctypes.data_as(POINTER(ctype))
@@ -141,6 +151,72 @@ def l2norm(x: np.ndarray, width: int, scale: float, eps: float = 1e-6) -> np.nda
     lib().oracle_l2norm(_ptr(x, c_float), _ptr(out, c_float), c_size_t(x.size // width),
                         c_uint(width), c_float(eps), c_float(scale))
     return out
+
+
+def delta_gates(a: np.ndarray, b: np.ndarray, a_log: np.ndarray, dt_bias: np.ndarray):
+    """deltaGates on fp16 inputs a, b [rows][heads] -> (beta, decay) fp32."""
+    af = f16_bits_to_f32(_as_bits(a))
+    bf = f16_bits_to_f32(_as_bits(b))
+    heads = af.shape[-1]
+    beta = np.empty(af.shape, np.float32)
+    decay = np.empty(af.shape, np.float32)
+    a_log = np.ascontiguousarray(a_log, np.float32)
+    dt_bias = np.ascontiguousarray(dt_bias, np.float32)
+    lib().oracle_delta_gates(_ptr(af, c_float), _ptr(bf, c_float), _ptr(a_log, c_float),
+                             _ptr(dt_bias, c_float), c_size_t(af.size // heads), c_uint(heads),
+                             _ptr(beta, c_float), _ptr(decay, c_float))
+    return beta, decay
+
+
+def norm_rope(x: np.ndarray, weight, past: int, rotary_dim: int, theta: float,
+              eps: float = 1e-6, head_dim: int | None = None, output=None, output_start: int = 0):
+    """normRope / partialRope over x [batch][tokens][heads][width] fp16 (the
+    row is the first head_dim of each width-wide head); weight None skips the
+    norm.  Writes rows output_start.. of `output` [batch][rows][heads][head_dim]
+    (a copy is returned), or a fresh [batch][tokens][heads][head_dim] array."""
+    x = np.ascontiguousarray(_as_bits(x))
+    batch, tokens, heads, width = x.shape
+    head_dim = head_dim or width
+    if output is None:
+        out = np.zeros((batch, tokens, heads, head_dim), np.uint16)
+    else:
+        out = np.ascontiguousarray(_as_bits(output)).copy()
+    p = RopeParams(tokens, heads, head_dim, rotary_dim, width, past, output_start, eps, theta)
+    w = None if weight is None else np.ascontiguousarray(weight, np.float32)
+    lib().oracle_norm_rope(ctypes.byref(p), c_uint(batch), _ptr(x, c_uint16),
+                           c_size_t(x[0].size), None if w is None else _ptr(w, c_float),
+                           _ptr(out, c_uint16), c_size_t(out[0].size))
+    return out.view(np.float16)
+
+
+def causal_conv(x: np.ndarray, weight: np.ndarray, history: np.ndarray, apply_silu: bool):
+    """causalConv over x [batch][tokens][channels] fp16 with weight
+    [channels][kernel] fp16 and history [batch][channels][kernel-1] fp16.
+    Returns (out fp16, the advanced history)."""
+    x = np.ascontiguousarray(_as_bits(x))
+    w = np.ascontiguousarray(_as_bits(weight))
+    hist = np.ascontiguousarray(_as_bits(history)).copy()
+    batch, tokens, channels = x.shape
+    out = np.empty_like(x)
+    p = ConvParams(tokens, channels, w.shape[1], 1 if apply_silu else 0)
+    lib().oracle_causal_conv(ctypes.byref(p), c_uint(batch), _ptr(x, c_uint16),
+                             c_size_t(x[0].size), _ptr(w, c_uint16), _ptr(hist, c_uint16),
+                             c_size_t(hist[0].size), _ptr(out, c_uint16), c_size_t(out[0].size))
+    return out.view(np.float16), hist.view(np.float16)
+
+
+def delta_prepare(qkv, weight, history, key_heads, key_dim, value_heads, value_dim, eps=1e-6):
+    """The DeltaNet block's q, k (fp32) and v (fp16) from its qkv projection:
+    causalConv with SiLU, the Slices, l2NormF32 of q (scale 1/sqrt(keyDim))
+    and k (scale 1) (Qwen35ModelBuilder.cpp:146-157).  Returns (q, k, v,
+    advanced history)."""
+    conv, hist = causal_conv(qkv, weight, history, True)
+    kw = key_heads * key_dim
+    cf = f16_bits_to_f32(conv.view(np.uint16))
+    q = l2norm(cf[..., :kw], key_dim, 1.0 / np.sqrt(np.float32(key_dim)), eps)
+    k = l2norm(cf[..., kw:2 * kw], key_dim, 1.0, eps)
+    v = np.ascontiguousarray(conv[..., 2 * kw:2 * kw + value_heads * value_dim])
+    return q, k, v, hist
 
 
 def reference_shim():
