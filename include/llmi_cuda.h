@@ -199,7 +199,8 @@ typedef struct {
  * keys, pass the key cache and outputStart = past (the step's cacheAppend).
  * x = half(x * rsqrt(mean(x^2) + epsilon) * (1 + weight)), then pairs
  * (i, i + rotaryDim/2) rotate by (past + token) / theta^(2i/rotaryDim) with
- * fp16-rounded cos/sin.  headDim <= 1024, rotaryDim even and <= headDim. */
+ * fp16-rounded cos/sin.  headDim <= 1024, rotaryDim even, <= headDim and
+ * <= 256. */
 int llmi_cuda_norm_rope(const llmi_rope_params *p, unsigned batch, const uint16_t *input,
                         size_t input_stride, const float *weight, uint16_t *output,
                         size_t output_stride, void *stream);

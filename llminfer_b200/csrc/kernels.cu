@@ -757,7 +757,8 @@ int rope_common(const char *op, const llmi_rope_params *p, unsigned batch, const
   if (!batch || !p->tokens || !p->heads || !p->headDim)
     return fail(LLMI_INVALID_ARGUMENT, "%s: sizes must be positive", op);
   if (p->headDim > unsigned(producers::kRopeMaxDim) || p->rotaryDim % 2 ||
-      p->rotaryDim > p->headDim || p->headStride < p->headDim)
+      p->rotaryDim > p->headDim || p->rotaryDim > unsigned(producers::kRopeMaxRotary) ||
+      p->headStride < p->headDim)
     return fail(LLMI_UNSUPPORTED, "%s: headDim %u, rotaryDim %u, headStride %u", op, p->headDim,
                 p->rotaryDim, p->headStride);
   const uint64_t rows = uint64_t(p->tokens) * p->heads;
@@ -782,10 +783,13 @@ int rope_common(const char *op, const llmi_rope_params *p, unsigned batch, const
   a.theta = p->theta;
   const bool vec = p->headDim % 8 == 0 && p->headStride % 8 == 0 && aligned16(input) &&
                    aligned16(output) && input_stride % 8 == 0 && output_stride % 8 == 0;
-  const unsigned grid = grid_for(rows * batch, producers::kRopeWarps);
+  const unsigned grid = grid_for(uint64_t(p->tokens) * batch, producers::kRopeWarps);
   cudaStream_t s = as_stream(stream);
-  if (vec)
-    producers::norm_rope<true><<<grid, 32 * producers::kRopeWarps, 0, s>>>(a);
+  if (vec && p->headDim <= 256)
+    producers::norm_rope<true, 1><<<grid, 32 * producers::kRopeWarps, 0, s>>>(a);
+  else if (vec)
+    producers::norm_rope<true, producers::kRopeMaxDim / 256>
+        <<<grid, 32 * producers::kRopeWarps, 0, s>>>(a);
   else
     producers::norm_rope<false><<<grid, 32 * producers::kRopeWarps, 0, s>>>(a);
   return launched(op);
@@ -923,8 +927,18 @@ extern "C" int llmi_cuda_delta_prepare(const llmi_delta_prep_params *p, unsigned
   a.k = k;
   a.v = reinterpret_cast<__half *>(v);
   cudaStream_t s = as_stream(stream);
-  const uint64_t rows = uint64_t(batch) * p->tokens * (2 * p->keyHeads + p->valueHeads);
-  producers::delta_prepare<<<grid_for(rows, 8), 256, 0, s>>>(a);
+  const unsigned heads = 2 * p->keyHeads + p->valueHeads;
+  const bool tiled = p->keyDim == 128 && p->valueDim == 128 && p->kernelSize == 4 &&
+                     aligned16(qkv) && aligned16(conv_weight) && aligned16(q) && aligned16(k) &&
+                     aligned16(v) && (batch == 1 || qkv_stride % 8 == 0) && batch <= 65535;
+  if (tiled) {
+    const dim3 grid((p->tokens + producers::kPrepTokens - 1) / producers::kPrepTokens,
+                    (heads + 7) / 8, batch);
+    producers::delta_prepare_tiled<<<grid, 256, 0, s>>>(a);
+  } else {
+    const uint64_t rows = uint64_t(batch) * p->tokens * heads;
+    producers::delta_prepare<<<grid_for(rows, 8), 256, 0, s>>>(a);
+  }
   if (int e = launched("deltaPrepare"))
     return e;
   return advance_history(a.conv, history, s);

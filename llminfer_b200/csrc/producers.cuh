@@ -22,7 +22,9 @@
 namespace llmi {
 namespace producers {
 
-__device__ __forceinline__ float logistic(float x) { return 1.0f / (1.0f + expf(-x)); }
+// 1 / (1 + e^-x): the correctly rounded reciprocal equals the IEEE quotient
+// 1.0f / y bit for bit, in fewer instructions.
+__device__ __forceinline__ float logistic(float x) { return __frcp_rn(1.0f + expf(-x)); }
 __device__ __forceinline__ float silu(float x) { return x * logistic(x); }
 __device__ __forceinline__ float stable_softplus(float x) {
   const float e = expf(-fabsf(x));
@@ -53,76 +55,158 @@ struct RopeArgs {
   float epsilon, theta;
 };
 
-// One warp per (sequence, token, head) row.  Row r of a sequence reads
-// input + r * head_stride and writes output + (output_start * heads + r) *
-// head_dim (for k, the cache rows of this step).  kVec: head_dim % 8 == 0
-// and 16-byte aligned rows (uint4 loads and stores).
-template <bool kVec>
-__global__ void __launch_bounds__(32 * kRopeWarps) norm_rope(const RopeArgs a) {
+// One warp per (sequence, token): the token's rotary angles are computed
+// once (pair i by lane i % 32, so at most kRopeMaxPairs / 32 per lane, in
+// registers) and then every head row of the token is processed.  Head h of
+// the token reads input + (token * heads + h) * head_stride and writes
+// output + ((output_start + token) * heads + h) * head_dim (for k, the
+// cache rows of this step).  kVec: head_dim % 8 == 0 and 16-byte aligned
+// rows (uint4 loads and stores).
+constexpr int kRopeMaxRotary = 256;  // rotary dims (Qwen3.5 rotates 64)
+constexpr int kRopeMaxPairs = kRopeMaxRotary / 2;
+template <bool kVec, int kChunks = 1>
+__global__ void __launch_bounds__(32 * kRopeWarps, kChunks == 1 ? 4 : 2)
+    norm_rope(const RopeArgs a) {
   __shared__ __align__(16) __half rows[kRopeWarps][kRopeMaxDim];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint64_t rows_per_seq = uint64_t(a.tokens) * a.heads;
   const uint64_t g = uint64_t(blockIdx.x) * kRopeWarps + warp;
-  if (g >= rows_per_seq * a.batch)
+  if (g >= uint64_t(a.tokens) * a.batch)
     return;  // whole warps only
-  const uint32_t seq = uint32_t(g / rows_per_seq), row = uint32_t(g % rows_per_seq);
-  const __half *in = a.input + seq * a.input_stride + size_t(row) * a.head_stride;
-  __half *out = a.output + seq * a.output_stride +
-                (size_t(a.output_start) * a.heads + row) * a.head_dim;
+  const uint32_t seq = uint32_t(g / a.tokens), token = uint32_t(g % a.tokens);
   __half *x = rows[warp];
-  const unsigned D = a.head_dim;
+  const unsigned D = a.head_dim, half_r = a.rotary_dim / 2;
 
-  // Normalised row (fp16, as rmsNorm writes it) into the warp's row buffer.
-  if (a.weight) {
-    float sum = 0.f;
-    if (kVec) {
-      for (unsigned i = lane * 8; i < D; i += 256) {
-        const uint4 w = *reinterpret_cast<const uint4 *>(in + i);
-        const __half *h = reinterpret_cast<const __half *>(&w);
+  // cos and sin of this lane's pairs, rounded to fp16 (rotatePair).
+  constexpr int kPerLane = kRopeMaxPairs / 32;
+  float cs[kPerLane], sn[kPerLane];
+  const float position = float(a.past + token);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float v = __half2float(h[e]);
-          sum = fmaf(v, v, sum);
-        }
-        *reinterpret_cast<uint4 *>(x + i) = w;
+  for (int k = 0; k < kPerLane; ++k) {
+    const unsigned i = lane + 32 * k;
+    if (i < half_r) {
+      const float phase = position / powf(a.theta, 2.0f * float(i) / float(a.rotary_dim));
+      cs[k] = round_half(cosf(phase));
+      sn[k] = round_half(sinf(phase));
+    }
+  }
+
+  auto row_in = [&](unsigned h) {
+    return a.input + seq * a.input_stride + (uint64_t(token) * a.heads + h) * a.head_stride;
+  };
+  if constexpr (kVec) {
+    // Lane l holds elements 8l + 256k .. +8 (k < kChunks, head_dim <= 256
+    // kChunks) of every row in registers, with (1 + w) for them; the next
+    // head's row is loaded while this one is processed.
+    float wp1[kChunks][8];
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const unsigned i = 256 * k + 8 * lane + e;
+        wp1[k][e] = (a.weight && i < D) ? 1.0f + a.weight[i] : 1.0f;
       }
-    } else {
+    uint4 cur[kChunks], nxt[kChunks];
+    auto load = [&](unsigned h, uint4 (&r)[kChunks]) {
+      const __half *in = row_in(h);
+#pragma unroll
+      for (int k = 0; k < kChunks; ++k)
+        if (256 * k + 8 * lane < D)
+          r[k] = *reinterpret_cast<const uint4 *>(in + 256 * k + 8 * lane);
+    };
+    load(0, cur);
+    for (unsigned h = 0; h < a.heads; ++h) {
+      if (h + 1 < a.heads)
+        load(h + 1, nxt);
+      float scale = 1.f;
+      if (a.weight) {
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < kChunks; ++k)
+          if (256 * k + 8 * lane < D) {
+            const __half *hv = reinterpret_cast<const __half *>(&cur[k]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float v = __half2float(hv[e]);
+              sum = fmaf(v, v, sum);
+            }
+          }
+        sum = warp_sum(sum);
+        scale = rsqrtf(sum / float(D) + a.epsilon);
+      }
+#pragma unroll
+      for (int k = 0; k < kChunks; ++k)
+        if (256 * k + 8 * lane < D) {
+          uint4 o = cur[k];
+          if (a.weight) {
+            const __half *hv = reinterpret_cast<const __half *>(&cur[k]);
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              v[e] = __half2float(hv[e]) * scale * wp1[k][e];
+            o = make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]),
+                           pack_half2(v[4], v[5]), pack_half2(v[6], v[7]));
+          }
+          *reinterpret_cast<uint4 *>(x + 256 * k + 8 * lane) = o;
+        }
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < kPerLane; ++k) {
+        const unsigned i = lane + 32 * k;
+        if (i < half_r) {
+          const unsigned j = i + half_r;
+          const float xv = __half2float(x[i]), yv = __half2float(x[j]);
+          x[i] = __float2half_rn(round_half(xv * cs[k]) - round_half(yv * sn[k]));
+          x[j] = __float2half_rn(round_half(yv * cs[k]) + round_half(xv * sn[k]));
+        }
+      }
+      __syncwarp();
+      __half *out = a.output + seq * a.output_stride +
+                    (uint64_t(a.output_start) * a.heads + uint64_t(token) * a.heads + h) * D;
+#pragma unroll
+      for (int k = 0; k < kChunks; ++k)
+        if (256 * k + 8 * lane < D)
+          *reinterpret_cast<uint4 *>(out + 256 * k + 8 * lane) =
+              *reinterpret_cast<const uint4 *>(x + 256 * k + 8 * lane);
+      __syncwarp();  // the row buffer is reused by the next head
+#pragma unroll
+      for (int k = 0; k < kChunks; ++k)
+        cur[k] = nxt[k];
+    }
+  } else {
+  for (unsigned h = 0; h < a.heads; ++h) {
+    const __half *in = row_in(h);
+    __half *out = a.output + seq * a.output_stride +
+                  (uint64_t(a.output_start) * a.heads + uint64_t(token) * a.heads + h) * D;
+    if (a.weight) {
+      float sum = 0.f;
       for (unsigned i = lane; i < D; i += 32) {
         const float v = __half2float(in[i]);
         sum = fmaf(v, v, sum);
+      }
+      sum = warp_sum(sum);
+      const float scale = rsqrtf(sum / float(D) + a.epsilon);
+      for (unsigned i = lane; i < D; i += 32)
+        x[i] = __float2half_rn(__half2float(in[i]) * scale * (1.0f + a.weight[i]));
+    } else {
+      for (unsigned i = lane; i < D; i += 32)
         x[i] = in[i];
+    }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < kPerLane; ++k) {
+      const unsigned i = lane + 32 * k;
+      if (i < half_r) {
+        const unsigned j = i + half_r;
+        const float xv = __half2float(x[i]), yv = __half2float(x[j]);
+        x[i] = __float2half_rn(round_half(xv * cs[k]) - round_half(yv * sn[k]));
+        x[j] = __float2half_rn(round_half(yv * cs[k]) + round_half(xv * sn[k]));
       }
     }
-    sum = warp_sum(sum);
-    const float scale = rsqrtf(sum / float(D) + a.epsilon);
     __syncwarp();
     for (unsigned i = lane; i < D; i += 32)
-      x[i] = __float2half_rn(__half2float(x[i]) * scale * (1.0f + a.weight[i]));
-  } else {
-    for (unsigned i = lane; i < D; i += 32)
-      x[i] = in[i];
-  }
-  __syncwarp();
-
-  // Rotary pairs (i, i + R/2), R = rotary_dim, at position past + token.
-  const unsigned half_r = a.rotary_dim / 2;
-  const float position = float(a.past + row / a.heads);
-  for (unsigned i = lane; i < half_r; i += 32) {
-    const unsigned j = i + half_r;
-    const float phase = position / powf(a.theta, 2.0f * float(i) / float(a.rotary_dim));
-    const float c = round_half(cosf(phase)), s = round_half(sinf(phase));
-    const float xv = __half2float(x[i]), yv = __half2float(x[j]);
-    // Pairs are disjoint, so each lane reads and writes only its own.
-    x[i] = __float2half_rn(round_half(xv * c) - round_half(yv * s));
-    x[j] = __float2half_rn(round_half(yv * c) + round_half(xv * s));
-  }
-  __syncwarp();
-  if (kVec) {
-    for (unsigned i = lane * 8; i < D; i += 256)
-      *reinterpret_cast<uint4 *>(out + i) = *reinterpret_cast<const uint4 *>(x + i);
-  } else {
-    for (unsigned i = lane; i < D; i += 32)
       out[i] = x[i];
+    __syncwarp();  // the row buffer is reused by the next head
+  }
   }
 }
 
@@ -238,7 +322,7 @@ __global__ void __launch_bounds__(256) delta_prepare(const PrepArgs a) {
   }
   sum = warp_sum(sum);
   const bool is_q = h < a.key_heads;
-  const float factor = rsqrtf(sum + a.epsilon) * (is_q ? rsqrtf(float(a.key_dim)) : 1.0f);
+  const float factor = rsqrtf(sum + a.epsilon) * (is_q ? 1.0f / sqrtf(float(a.key_dim)) : 1.0f);
   float *out = (is_q ? a.q : a.k) +
                (size_t(seq) * a.conv.tokens + t) * a.key_heads * a.key_dim +
                (is_q ? h : h - a.key_heads) * a.key_dim;
@@ -246,6 +330,118 @@ __global__ void __launch_bounds__(256) delta_prepare(const PrepArgs a) {
   for (int e = 0; e < 8; ++e)
     if (lane + 32 * e < width)
       out[lane + 32 * e] = y[e] * factor;
+}
+
+// Tiled form for 128-wide heads and 4 conv taps (the Qwen3.5 shape): one warp
+// owns one head for kPrepTokens consecutive tokens.  Lane l holds channels
+// 4l..4l+3 of the head: their 4 x 4 taps in registers, and a sliding window
+// of the last three input rows (8-byte loads), so every input row is read
+// once per tile and every weight once per warp.  The tap sums keep the
+// reference's order.  Grid (token tiles, ceil(heads / 8), batch).
+constexpr int kPrepTokens = 32;
+__global__ void __launch_bounds__(256, 4) delta_prepare_tiled(const PrepArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned heads = 2 * a.key_heads + a.value_heads;
+  const unsigned h = blockIdx.y * 8 + warp;
+  if (h >= heads)
+    return;  // whole warps only
+  const uint32_t seq = blockIdx.z;
+  const uint32_t W = a.conv.channels;
+  const uint32_t t0 = blockIdx.x * kPrepTokens;
+  const uint32_t t1 = min(t0 + uint32_t(kPrepTokens), a.conv.tokens);
+  const bool is_v = h >= 2 * a.key_heads;
+  const uint32_t c = (is_v ? 2 * a.key_heads * 128 + (h - 2 * a.key_heads) * 128 : h * 128) +
+                     4 * lane;
+  const __half *in = a.conv.input + seq * a.conv.input_stride;
+  const __half *hist = a.conv.history + seq * a.conv.history_stride;
+
+  float w[4][4];  // [channel][tap]
+  {
+    const uint4 *wp = reinterpret_cast<const uint4 *>(a.conv.weight + size_t(c) * 4);
+    const uint4 w0 = wp[0], w1 = wp[1];
+    const __half *h0 = reinterpret_cast<const __half *>(&w0);
+    const __half *h1 = reinterpret_cast<const __half *>(&w1);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      w[j / 4][j % 4] = __half2float(h0[j]);
+      w[2 + j / 4][j % 4] = __half2float(h1[j]);
+    }
+  }
+  auto load_row = [&](int tau, float (&r)[4]) {
+    if (tau >= 0) {
+      const uint2 v = *reinterpret_cast<const uint2 *>(in + size_t(tau) * W + c);
+      const __half *hv = reinterpret_cast<const __half *>(&v);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        r[e] = __half2float(hv[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        r[e] = __half2float(hist[size_t(c + e) * 3 + size_t(tau + 3)]);
+    }
+  };
+  float x3[4], x2[4], x1[4];  // rows t-3, t-2, t-1
+  load_row(int(t0) - 3, x3);
+  load_row(int(t0) - 2, x2);
+  load_row(int(t0) - 1, x1);
+  const bool is_q = h < a.key_heads;
+  const float scale = is_q ? 1.0f / sqrtf(float(a.key_dim)) : 1.0f;
+  // Rows are loaded kPrepAhead tokens at a time, so that many loads are in
+  // flight per lane before the first is used.
+  constexpr int kPrepAhead = 4;
+  uint2 ahead[kPrepAhead];
+  for (uint32_t t = t0; t < t1; ++t) {
+    const uint32_t slot = (t - t0) % kPrepAhead;
+    if (slot == 0) {
+#pragma unroll
+      for (int u = 0; u < kPrepAhead; ++u)
+        if (t + u < t1)
+          ahead[u] = *reinterpret_cast<const uint2 *>(in + size_t(t + u) * W + c);
+    }
+    float x0[4];
+    {
+      uint2 v = ahead[0];
+#pragma unroll
+      for (int u = 1; u < kPrepAhead; ++u)
+        if (slot == uint32_t(u))
+          v = ahead[u];
+      const __half *hv = reinterpret_cast<const __half *>(&v);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        x0[e] = __half2float(hv[e]);
+    }
+    float y[4], sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float acc = x0[e] * w[e][3];
+      acc = fmaf(x3[e], w[e][0], acc);
+      acc = fmaf(x2[e], w[e][1], acc);
+      acc = fmaf(x1[e], w[e][2], acc);
+      y[e] = round_half(silu(round_half(acc)));
+      sum = fmaf(y[e], y[e], sum);
+    }
+    const size_t tok = size_t(seq) * a.conv.tokens + t;
+    if (is_v) {
+      uint2 o;
+      o.x = pack_half2(y[0], y[1]);
+      o.y = pack_half2(y[2], y[3]);
+      *reinterpret_cast<uint2 *>(a.v + tok * a.value_heads * 128 +
+                                 (h - 2 * a.key_heads) * 128 + 4 * lane) = o;
+    } else {
+      sum = warp_sum(sum);
+      const float factor = rsqrtf(sum + a.epsilon) * scale;
+      float *out = (is_q ? a.q : a.k) + tok * a.key_heads * 128 +
+                   (is_q ? h : h - a.key_heads) * 128 + 4 * lane;
+      *reinterpret_cast<float4 *>(out) =
+          make_float4(y[0] * factor, y[1] * factor, y[2] * factor, y[3] * factor);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      x3[e] = x2[e];
+      x2[e] = x1[e];
+      x1[e] = x0[e];
+    }
+  }
 }
 
 // ---- L2Norm (fp16 rows -> fp32) and DeltaGates ---------------------------------
