@@ -19,7 +19,8 @@ Keys of the line beyond the base contract:
   e2e           the same step through the C-ABI calls with pinned host
                 buffers: H2D of q and the new rows, D2H of the output, timed
   secondary     the other kernels of the path on their benchmark configs
-                (C1 prefill, C4 DeltaNet step, C3 DeltaNet prefill), each
+                (C1 prefill, C4 DeltaNet step, C3 DeltaNet prefill) and the
+                producers of its operands at the C5 layer shapes, each
                 run whole on every GPU (aggregate over N GPUs, max-over-ranks
                 time)
   stack         the C5 hybrid stack (llminfer_b200/stack.py): 24 DeltaNet +
@@ -517,6 +518,50 @@ def run_secondary(torch, ops, device, peaks, dist):
     res.append({"workload": "C3 DeltaNet prefill B=4 T=4096 per GPU (graphDeltaUpdate, chunked)",
                 "ms": round(med, 4), "value": round(gbs * N, 1), "unit": "GB/s",
                 "tflops_cost_model": round(2 * cost[1] * N / (med / 1e3) / 1e12, 3),
+                "frac_of_hbm_peak": round(gbs / peaks["hbm_gbs"], 4)})
+    del qd, kd, vd, beta, decay, state, od
+    # Producers at the C5 layer shapes (B=16 per GPU, T=8192): q/k RmsNorm +
+    # partial RoPE of a GQA layer (k into the cache), and a DeltaNet layer's
+    # conv + SiLU + q/k L2 norm and gates.  Bytes: each operand read and
+    # written once.
+    B, T, D = 16, 8192, 256
+    qg = torch.randn(B, T, 16, 2 * D, generator=g, device=device).half()
+    kr = torch.randn(B, T, 4, D, generator=g, device=device).half()
+    wq = (0.1 * torch.randn(D, generator=g, device=device)).float()
+    wk = (0.1 * torch.randn(D, generator=g, device=device)).float()
+    qo = torch.empty(B, T, 16, D, dtype=torch.float16, device=device)
+    cache = torch.empty(B, T, 4, D, dtype=torch.float16, device=device)
+
+    def rope():
+        ops.norm_rope(qg, wq, 0, D // 4, 1e7, head_dim=D, out=qo)
+        ops.norm_rope(kr, wk, 0, D // 4, 1e7, out=cache, output_start=0)
+
+    med, best = time_op(torch, rope, dist, reps=5, warmup=2)
+    gbs = 2 * (qo.numel() + cache.numel()) * 2 / (med / 1e3) / 1e9
+    res.append({"workload": "q/k RmsNorm + partial RoPE of a GQA layer, k into the cache, "
+                            "C5 shape B=16 T=8192 per GPU (normRope)",
+                "ms": round(med, 4), "value": round(gbs * N, 1), "unit": "GB/s",
+                "frac_of_hbm_peak": round(gbs / peaks["hbm_gbs"], 4)})
+    del qg, kr, qo, cache
+    W = 2 * Hk * dk + Hv * dv
+    qkv = torch.randn(B, T, W, generator=g, device=device).half()
+    wconv = (0.5 * torch.randn(W, 4, generator=g, device=device)).half()
+    hist = torch.zeros(B, W, 3, dtype=torch.float16, device=device)
+    ga = torch.randn(B, T, Hv, generator=g, device=device).half()
+    gb = torch.randn(B, T, Hv, generator=g, device=device).half()
+    a_log = torch.randn(Hv, generator=g, device=device).float()
+    dt_bias = torch.randn(Hv, generator=g, device=device).float()
+
+    def prep():
+        ops.delta_prepare(qkv, wconv, hist, Hk, dk, Hv, dv)
+        ops.delta_gates(ga, gb, a_log, dt_bias)
+
+    med, best = time_op(torch, prep, dist, reps=5, warmup=2)
+    nbytes = B * T * (W * 2 + 2 * Hk * dk * 4 + Hv * dv * 2 + Hv * (2 * 2 + 2 * 4))
+    gbs = nbytes / (med / 1e3) / 1e9
+    res.append({"workload": "DeltaNet layer inputs: conv + SiLU + q/k L2 norm and gates, "
+                            "C5 shape B=16 T=8192 per GPU (deltaPrepare, deltaGates)",
+                "ms": round(med, 4), "value": round(gbs * N, 1), "unit": "GB/s",
                 "frac_of_hbm_peak": round(gbs / peaks["hbm_gbs"], 4)})
     return res
 
