@@ -123,6 +123,126 @@ __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v128(const Args a) {
     st_stream_f4(S + size_t(warp + kRecWarps * r) * DV + lane * 4, s[r]);
 }
 
+// The same update with the value columns split into blocks of 32: one CTA
+// per (sequence, value head, block), 16 KiB of state for dk = 128, so small
+// batches still give every SM several CTAs (at batch 16 the 128-column form
+// has 512 CTAs and runs at a third of HBM bandwidth).  Lane l holds columns
+// 4(l % 8)..+3 of the block for rows w*4 + l/8 + 32p; each warp load covers
+// four 128-byte row segments.  Row sums: per lane, then across the four row
+// lanes of a warp (shuffles), then across warps (shared memory).
+// Grid (Hv * dv / 32, batch), 256 threads; dk multiple of 32, <= 128.
+template <int DK>
+__global__ void __launch_bounds__(kRecWarps * 32) recurrent_v32(const Args a) {
+  constexpr int R = DK / 32;  // row passes per thread
+  constexpr int DV = 128, kCols = 32;
+  __shared__ float4 red_pred[kRecWarps][8];
+  __shared__ float4 red_out[kRecWarps][8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cg = lane & 7, rs = lane >> 3;
+  const uint32_t vh = blockIdx.x / (DV / kCols), blk = blockIdx.x % (DV / kCols);
+  const uint32_t seq = blockIdx.y, kh = vh / a.group;
+  const uint32_t col = blk * kCols + 4 * cg;  // this lane's first column within the head
+  float *S = a.state + (size_t(seq) * a.value_heads + vh) * DK * DV;
+  auto row_of = [&](int p) { return warp * 4 + rs + 32 * p; };
+
+  float4 s[R];
+#pragma unroll
+  for (int p = 0; p < R; ++p)
+    s[p] = ld_stream_f4(S + size_t(row_of(p)) * DV + col);
+
+  const size_t key_width = size_t(a.key_heads) * DK;
+  const size_t value_width = size_t(a.value_heads) * DV;
+  for (uint32_t t = 0; t < a.tokens; ++t) {
+    const size_t tok = size_t(seq) * a.tokens + t;
+    const float *kt = a.k + tok * key_width + size_t(kh) * DK;
+    const float *qt = a.q + tok * key_width + size_t(kh) * DK;
+    const float dec = __ldg(a.decay + tok * a.value_heads + vh);
+    const float bet = __ldg(a.beta + tok * a.value_heads + vh);
+    const uint2 vraw = __ldg(reinterpret_cast<const uint2 *>(a.v + tok * value_width + vh * DV + col));
+    const float2 v01 = __half22float2(*reinterpret_cast<const __half2 *>(&vraw.x));
+    const float2 v23 = __half22float2(*reinterpret_cast<const __half2 *>(&vraw.y));
+    float kr[R], qr[R];
+#pragma unroll
+    for (int p = 0; p < R; ++p) {
+      kr[p] = __ldg(kt + row_of(p));
+      qr[p] = __ldg(qt + row_of(p));
+    }
+    float4 pp = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < R; ++p) {
+      pp.x = fmaf(s[p].x * dec, kr[p], pp.x);
+      pp.y = fmaf(s[p].y * dec, kr[p], pp.y);
+      pp.z = fmaf(s[p].z * dec, kr[p], pp.z);
+      pp.w = fmaf(s[p].w * dec, kr[p], pp.w);
+    }
+#pragma unroll
+    for (int off = 8; off < 32; off <<= 1) {
+      pp.x += __shfl_xor_sync(0xffffffffu, pp.x, off);
+      pp.y += __shfl_xor_sync(0xffffffffu, pp.y, off);
+      pp.z += __shfl_xor_sync(0xffffffffu, pp.z, off);
+      pp.w += __shfl_xor_sync(0xffffffffu, pp.w, off);
+    }
+    if (rs == 0)
+      red_pred[warp][cg] = pp;
+    __syncthreads();
+    float4 pred = red_pred[0][cg];
+#pragma unroll
+    for (int w = 1; w < kRecWarps; ++w) {
+      const float4 x = red_pred[w][cg];
+      pred.x += x.x;
+      pred.y += x.y;
+      pred.z += x.z;
+      pred.w += x.w;
+    }
+    const float4 delta = make_float4((v01.x - pred.x) * bet, (v01.y - pred.y) * bet,
+                                     (v23.x - pred.z) * bet, (v23.y - pred.w) * bet);
+    float4 yp = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < R; ++p) {
+      s[p].x = fmaf(kr[p], delta.x, s[p].x * dec);
+      s[p].y = fmaf(kr[p], delta.y, s[p].y * dec);
+      s[p].z = fmaf(kr[p], delta.z, s[p].z * dec);
+      s[p].w = fmaf(kr[p], delta.w, s[p].w * dec);
+      yp.x = fmaf(s[p].x, qr[p], yp.x);
+      yp.y = fmaf(s[p].y, qr[p], yp.y);
+      yp.z = fmaf(s[p].z, qr[p], yp.z);
+      yp.w = fmaf(s[p].w, qr[p], yp.w);
+    }
+#pragma unroll
+    for (int off = 8; off < 32; off <<= 1) {
+      yp.x += __shfl_xor_sync(0xffffffffu, yp.x, off);
+      yp.y += __shfl_xor_sync(0xffffffffu, yp.y, off);
+      yp.z += __shfl_xor_sync(0xffffffffu, yp.z, off);
+      yp.w += __shfl_xor_sync(0xffffffffu, yp.w, off);
+    }
+    if (rs == 0)
+      red_out[warp][cg] = yp;
+    __syncthreads();
+    if (warp == 0 && rs == 0) {
+      float4 y = red_out[0][cg];
+#pragma unroll
+      for (int w = 1; w < kRecWarps; ++w) {
+        const float4 x = red_out[w][cg];
+        y.x += x.x;
+        y.y += x.y;
+        y.z += x.z;
+        y.w += x.w;
+      }
+      uint2 packed;
+      *reinterpret_cast<__half2 *>(&packed.x) = __floats2half2_rn(y.x, y.y);
+      *reinterpret_cast<__half2 *>(&packed.y) = __floats2half2_rn(y.z, y.w);
+      *reinterpret_cast<uint2 *>(a.out + tok * value_width + vh * DV + col) = packed;
+    }
+    // The reduction buffers are reused by the next token.
+    if (t + 1 < a.tokens)
+      __syncthreads();
+  }
+
+#pragma unroll
+  for (int p = 0; p < R; ++p)
+    st_stream_f4(S + size_t(row_of(p)) * DV + col, s[p]);
+}
+
 // Any (dk, dv): one thread per (sequence, value column), state in global
 // memory, the reference's column walk.  Used only for shapes outside the
 // fast kernels.

@@ -696,8 +696,21 @@ extern "C" int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch
   }
   const bool fast = p->valueDim == 128 && (p->keyDim == 128 || p->keyDim == 64) &&
                     aligned16(state) && aligned16(v) && batch <= 65535 &&
-                    p->valueHeads <= 2147483647u;
+                    p->valueHeads <= 2147483647u / 4;
   if (fast) {
+    DeviceInfo dev;
+    if (int e = current_device(dev))
+      return e;
+    // Fewer than four 128-column CTAs per SM: split the columns in four so
+    // that the state streams through more CTAs at once.
+    if (uint64_t(p->valueHeads) * batch < 4ull * uint64_t(dev.sm_count)) {
+      dim3 grid(p->valueHeads * 4, batch);
+      if (p->keyDim == 128)
+        delta::recurrent_v32<128><<<grid, delta::kRecWarps * 32, 0, s>>>(a);
+      else
+        delta::recurrent_v32<64><<<grid, delta::kRecWarps * 32, 0, s>>>(a);
+      return launched("graphDeltaUpdate (recurrent, registers, 32-column blocks)");
+    }
     dim3 grid(p->valueHeads, batch);
     if (p->keyDim == 128)
       delta::recurrent_v128<128><<<grid, delta::kRecWarps * 32, 0, s>>>(a);

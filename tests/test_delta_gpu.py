@@ -40,6 +40,8 @@ def check(case, got_out, got_state):
 
 @pytest.mark.parametrize("batch,tokens,hk,dk,hv,dv,std", [
     (16, 1, 16, 128, 32, 128, 0.02),  # the recurrent-step config (C4), fewer sequences
+    (20, 1, 16, 128, 32, 128, 0.02),  # enough (sequence, head) pairs for 128-column CTAs
+    (24, 3, 8, 64, 32, 128, 0.02),    # the same, dk 64, a few tokens
     (3, 1, 16, 128, 32, 128, 0.0),
     (2, 1, 4, 64, 8, 128, 0.02),
     (2, 37, 2, 128, 4, 128, 0.02),    # one partial chunk (chunked kernel)
