@@ -17,6 +17,7 @@ struct AppendArgs {
 // 16-byte path: count, offset, strides and both bases are multiples of 8
 // halves.  One grid-stride loop over (sequence, vector).
 __global__ void __launch_bounds__(256) cache_append_v8(AppendArgs a) {
+  pdl_enter();
   const uint32_t vectors = a.count / 8;
   const uint64_t total = uint64_t(vectors) * a.batch;
   for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < total;
@@ -29,6 +30,7 @@ __global__ void __launch_bounds__(256) cache_append_v8(AppendArgs a) {
 }
 
 __global__ void __launch_bounds__(256) cache_append_scalar(AppendArgs a) {
+  pdl_enter();
   const uint64_t total = uint64_t(a.count) * a.batch;
   for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < total;
        i += uint64_t(gridDim.x) * blockDim.x) {

@@ -33,6 +33,25 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 
 __device__ __forceinline__ void raise_error(unsigned bits) { atomicOr(&g_error_word, bits); }
 
+// Programmatic dependent launch (griddepcontrol).  A kernel launched with
+// programmatic stream serialization may become resident once every CTA of the
+// kernel before it has called launch_dependents() (or exited); wait_primary()
+// then blocks until that kernel has completed and its memory is visible.
+// Decode-path kernels call both at entry, before any global access or early
+// return: the next launch's set-up and CTA ramp overlap this one's tail, and
+// since every kernel waits for its predecessor before finishing, the chain
+// stays ordered.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_primary() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_enter() {
+  launch_dependents();
+  wait_primary();
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

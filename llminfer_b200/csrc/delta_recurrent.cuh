@@ -34,6 +34,7 @@ constexpr int kRecWarps = 8;
 // dv == 128, dk == DK (multiple of 8, <= 128).  Grid (Hv, batch), 256 threads.
 template <int DK>
 __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v128(const Args a) {
+  pdl_enter();
   constexpr int R = DK / kRecWarps;  // state rows per warp
   constexpr int DV = 128;
   __shared__ float4 red_pred[kRecWarps][32];
@@ -133,6 +134,7 @@ __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v128(const Args a) {
 // Grid (Hv * dv / 32, batch), 256 threads; dk multiple of 32, <= 128.
 template <int DK>
 __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v32(const Args a) {
+  pdl_enter();
   constexpr int R = DK / 32;  // row passes per thread
   constexpr int DV = 128, kCols = 32;
   __shared__ float4 red_pred[kRecWarps][8];
@@ -247,6 +249,7 @@ __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v32(const Args a) {
 // memory, the reference's column walk.  Used only for shapes outside the
 // fast kernels.
 __global__ void __launch_bounds__(128) recurrent_generic(const Args a) {
+  pdl_enter();
   const uint32_t value_width = a.value_heads * a.value_dim;
   const uint64_t total = uint64_t(a.batch) * value_width;
   const uint64_t c = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x;

@@ -74,15 +74,6 @@ __host__ __device__ inline uint32_t record_floats(uint32_t group, uint32_t head_
   return (2 * group + group * head_dim + 3) & ~3u;
 }
 
-// griddepcontrol: the partial pass lets the merge grid launch early; the
-// merge waits for the partial grid's completion (and memory) before reading.
-__device__ __forceinline__ void launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-__device__ __forceinline__ void wait_primary() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
 struct Args {
   const __half *q;       // [batch][queryHeads][D]  (tokens == 1)
   const __half *k, *v;   // caches, sequence stride cache_stride
@@ -233,7 +224,7 @@ __global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
   volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(empty + STAGES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Partition pt = a.pt;  // heads == HKV, units = sequences
-  launch_dependents();
+  pdl_enter();  // before the first global read
   const uint32_t worker = blockIdx.x;
   const uint32_t total = pt.units * pt.tiles_per_unit;
   const uint32_t begin = min(total, worker * pt.tiles_per_worker);
@@ -337,7 +328,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
       reinterpret_cast<uint64_t *>(smem + WARPS * STAGES * Shape::kStageBytes) + warp * STAGES;
 
   const Partition pt = a.pt;
-  launch_dependents();
+  pdl_enter();  // before the first global read
   // heads == 1: this warp is a worker; otherwise the CTA is, and this warp
   // serves kv head `warp` of each sequence in the CTA's range.
   const bool grouped = pt.heads > 1;
@@ -432,6 +423,7 @@ __global__ void __launch_bounds__(128) partial_simt(const Args a) {
   constexpr int kMaxPerLane = 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Partition pt = a.pt;
+  pdl_enter();
   const uint32_t worker = blockIdx.x;  // tiles_per_worker == 1
   const uint32_t unit = worker / pt.tiles_per_unit, split = worker % pt.tiles_per_unit;
   if (unit >= pt.units)
@@ -504,6 +496,7 @@ constexpr int kMergeMaxGroup = 64;
 constexpr int kMergeMaxPerLane = 16;  // head_dim <= 512
 
 __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
+  launch_dependents();
   const Partition pt = a.pt;
   const uint32_t out_unit = blockIdx.x;  // seq * kv_heads + kvh
   const uint32_t seq = out_unit / a.kv_heads, kvh = out_unit % a.kv_heads;

@@ -74,6 +74,39 @@ int launched(const char *kernel) {
   return check_cuda(cudaGetLastError(), kernel);
 }
 
+// Decode-path kernels launch as programmatic dependents unless
+// LLMI_PROGRAMMATIC_LAUNCH=0 (read once per process); the kernels are the same
+// either way.
+bool programmatic_launch() {
+  static const bool on = [] {
+    const char *e = std::getenv("LLMI_PROGRAMMATIC_LAUNCH");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Launches a decode-path kernel as a programmatic dependent of the work before
+// it on the stream (the kernel calls pdl_enter() at entry): its launch and CTA
+// ramp overlap the previous kernel's tail.  Recorded into CUDA graphs as a
+// programmatic edge.
+template <typename... Params, typename... Actual>
+int launch_dependent(const char *name, void (*kernel)(Params...), dim3 grid, dim3 block,
+                     size_t smem, cudaStream_t stream, Actual &&...args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attr;
+  config.numAttrs = programmatic_launch() ? 1 : 0;
+  if (int e = check_cuda(cudaLaunchKernelEx(&config, kernel, std::forward<Actual>(args)...), name))
+    return e;
+  return launched(name);
+}
+
 int check_gqa(const llmi_gqa_params *p, unsigned batch, const void *q, const void *k,
               const void *v, size_t cache_stride, const void *out) {
   if (!p || !q || !k || !v || !out)
@@ -374,8 +407,8 @@ int launch_decode_rows(const DecodePlan &plan, const decode::Args &args, const D
   auto kernel = decode::partial_rows<D, HKV, STAGES>;
   if (int s = allow_smem(reinterpret_cast<const void *>(kernel), plan.smem, dev))
     return s;
-  kernel<<<plan.grid, plan.threads, plan.smem, stream>>>(args);
-  return launched("gqaScores (decode partial, row stream)");
+  return launch_dependent("gqaScores (decode partial, row stream)", kernel, plan.grid,
+                          plan.threads, plan.smem, stream, args);
 }
 
 template <int D, int WARPS, int STAGES>
@@ -384,8 +417,8 @@ int launch_decode_mma(const DecodePlan &plan, const decode::Args &args, const De
   auto kernel = decode::partial_mma<D, WARPS, STAGES>;
   if (int s = allow_smem(reinterpret_cast<const void *>(kernel), plan.smem, dev))
     return s;
-  kernel<<<plan.grid, plan.threads, plan.smem, stream>>>(args);
-  return launched("gqaScores (decode partial, tensor cores)");
+  return launch_dependent("gqaScores (decode partial, tensor cores)", kernel, plan.grid,
+                          plan.threads, plan.smem, stream, args);
 }
 
 }  // namespace
@@ -407,11 +440,8 @@ extern "C" int llmi_cuda_cache_append(const llmi_cache_params *p, unsigned batch
                    aligned16(cache) && (batch == 1 || (input_stride % 8 == 0 && cache_stride % 8 == 0));
   const uint64_t work = vec ? uint64_t(p->count / 8) * batch : uint64_t(p->count) * batch;
   const uint32_t grid = uint32_t(std::min<uint64_t>((work + 255) / 256, 4096));
-  if (vec)
-    cache_append_v8<<<grid, 256, 0, as_stream(stream)>>>(a);
-  else
-    cache_append_scalar<<<grid, 256, 0, as_stream(stream)>>>(a);
-  return launched("cacheAppend");
+  return launch_dependent("cacheAppend", vec ? cache_append_v8 : cache_append_scalar, grid, 256,
+                          0, as_stream(stream), a);
 }
 
 // ---- gqaFlashAttention ------------------------------------------------------------
@@ -535,26 +565,16 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
     status = launch_decode_mma<64, kWarps64, kStages64>(plan, a, dev, s);
     break;
   case DecodePlan::Simt:
-    decode::partial_simt<<<plan.grid, plan.threads, 0, s>>>(a);
-    status = launched("gqaScores (decode partial, CUDA cores)");
+    status = launch_dependent("gqaScores (decode partial, CUDA cores)", decode::partial_simt,
+                              plan.grid, plan.threads, 0, s, a);
     break;
   }
   if (status)
     return status;
-  // The merge is a programmatic dependent of the partial pass: it may be
-  // scheduled while the partial grid drains and waits for it on the device.
-  cudaLaunchConfig_t config = {};
-  config.gridDim = dim3(batch * p->kvHeads);
-  config.blockDim = dim3(decode::kMergeThreads);
-  config.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  config.attrs = attr;
-  config.numAttrs = 1;
-  if (int e = check_cuda(cudaLaunchKernelEx(&config, decode::merge, a), "gqaSoftmax (decode merge)"))
-    return e;
-  return launched("gqaSoftmax (decode merge)");
+  // The merge may be scheduled while the partial grid drains; it waits for
+  // it on the device.
+  return launch_dependent("gqaSoftmax (decode merge)", decode::merge, dim3(batch * p->kvHeads),
+                          dim3(decode::kMergeThreads), 0, s, a);
 }
 
 // ---- decode without a caller workspace ------------------------------------------------
@@ -704,23 +724,17 @@ extern "C" int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch
     // Fewer than four 128-column CTAs per SM: split the columns in four so
     // that the state streams through more CTAs at once.
     if (uint64_t(p->valueHeads) * batch < 4ull * uint64_t(dev.sm_count)) {
-      dim3 grid(p->valueHeads * 4, batch);
-      if (p->keyDim == 128)
-        delta::recurrent_v32<128><<<grid, delta::kRecWarps * 32, 0, s>>>(a);
-      else
-        delta::recurrent_v32<64><<<grid, delta::kRecWarps * 32, 0, s>>>(a);
-      return launched("graphDeltaUpdate (recurrent, registers, 32-column blocks)");
+      return launch_dependent("graphDeltaUpdate (recurrent, registers, 32-column blocks)",
+                              p->keyDim == 128 ? delta::recurrent_v32<128> : delta::recurrent_v32<64>,
+                              dim3(p->valueHeads * 4, batch), delta::kRecWarps * 32, 0, s, a);
     }
-    dim3 grid(p->valueHeads, batch);
-    if (p->keyDim == 128)
-      delta::recurrent_v128<128><<<grid, delta::kRecWarps * 32, 0, s>>>(a);
-    else
-      delta::recurrent_v128<64><<<grid, delta::kRecWarps * 32, 0, s>>>(a);
-    return launched("graphDeltaUpdate (recurrent, registers)");
+    return launch_dependent("graphDeltaUpdate (recurrent, registers)",
+                            p->keyDim == 128 ? delta::recurrent_v128<128> : delta::recurrent_v128<64>,
+                            dim3(p->valueHeads, batch), delta::kRecWarps * 32, 0, s, a);
   }
   const uint64_t columns = uint64_t(batch) * p->valueHeads * p->valueDim;
-  delta::recurrent_generic<<<uint32_t((columns + 127) / 128), 128, 0, s>>>(a);
-  return launched("graphDeltaUpdate (recurrent, generic)");
+  return launch_dependent("graphDeltaUpdate (recurrent, generic)", delta::recurrent_generic,
+                          dim3(uint32_t((columns + 127) / 128)), 128, 0, s, a);
 }
 
 // ---- device error word ---------------------------------------------------------------
