@@ -485,15 +485,18 @@ __global__ void __launch_bounds__(128) partial_simt(const Args a) {
 }
 
 // ---------------------------------------------------------------------------
-// Merge pass: one CTA per (sequence, kv head), one warp per query head.  The
-// warp reads every record's max and sum in parallel (lane i: record i),
-// reduces them with shuffles, then each lane sums its output dimensions over
-// the records with independent, coalesced loads.  Launched as a programmatic
-// dependent of the partial pass: it may start while that grid drains and
-// waits for it here.
+// Merge pass: one CTA per (sequence, kv head), one warp per query head.  Lane
+// i reads record i's max and sum once (records past 32 fold in with a loop),
+// the shuffled maximum gives every record's weight, and lane i's weight is
+// broadcast by shuffle where the outputs are summed.  The outputs are summed
+// with float4 loads, four records per round, so a unit's records cost a few
+// dependent load rounds rather than one per record.  Launched as a
+// programmatic dependent of the partial pass: it may start while that grid
+// drains and waits for it here.
 constexpr int kMergeThreads = 128;
 constexpr int kMergeMaxGroup = 64;
 constexpr int kMergeMaxPerLane = 16;  // head_dim <= 512
+constexpr int kMergeRound = 4;        // records per round of float4 loads
 
 __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   launch_dependents();
@@ -511,45 +514,102 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   auto record = [&](uint32_t i) {
     return a.records + record_index(pt, w_lo + i, unit, head) * a.record_floats;
   };
+  // float4 path: every head's output row starts on a 16-byte boundary
+  // (records are, and 2G and D are multiples of 4) and the fp16 output rows
+  // on an 8-byte one.
+  const bool vec = ((2 * G) & 3u) == 0 && (D & 3u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.out) & 7u) == 0;
   wait_primary();
   __half *out = a.out + (size_t(seq) * a.kv_heads * G + kvh * G) * D;
   for (uint32_t h = warp; h < G; h += kMergeThreads / 32) {
-    float top = -INFINITY;
-    for (uint32_t i = lane; i < n; i += 32)
+    float m_own = -INFINITY, l_own = 0.f;
+    if (uint32_t(lane) < n) {
+      const float *r = record(lane);
+      m_own = r[h];
+      l_own = r[G + h];
+    }
+    float top = m_own;
+    for (uint32_t i = lane + 32; i < n; i += 32)
       top = fmaxf(top, record(i)[h]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1)
       top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, off));
-    float sum = 0.f;
-    for (uint32_t i = lane; i < n; i += 32) {
+    const float w_own = uint32_t(lane) < n ? fast_exp2(m_own - top) : 0.f;
+    float sum = l_own * w_own;
+    for (uint32_t i = lane + 32; i < n; i += 32) {
       const float *r = record(i);
       sum = fmaf(r[G + h], fast_exp2(r[h] - top), sum);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1)
       sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    float acc[kMergeMaxPerLane];
+    // Record i's weight (i is uniform over the warp).
+    auto weight = [&](uint32_t i) {
+      const float w = __shfl_sync(0xffffffffu, w_own, int(i & 31u));
+      return i < 32 ? w : fast_exp2(record(i)[h] - top);
+    };
+    const float inv = 1.f / sum;
+    if (vec) {
+      // Lane l owns the float4 chunks l, l + 32, ... of the row (D <= 512).
+      float4 acc[kMergeMaxPerLane / 4];
 #pragma unroll
-    for (int k = 0; k < kMergeMaxPerLane; ++k)
-      acc[k] = 0.f;
+      for (int k = 0; k < kMergeMaxPerLane / 4; ++k)
+        acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (uint32_t i0 = 0; i0 < n; i0 += kMergeRound) {
+        float4 v[kMergeRound][kMergeMaxPerLane / 4];
+        float w[kMergeRound];
+#pragma unroll
+        for (int j = 0; j < kMergeRound; ++j) {
+          const uint32_t i = i0 + j;
+          w[j] = i < n ? weight(i) : 0.f;
+          const float4 *o =
+              reinterpret_cast<const float4 *>(record(min(i, n - 1)) + 2 * G + h * D);
+#pragma unroll
+          for (int k = 0; k < kMergeMaxPerLane / 4; ++k) {
+            const uint32_t c = lane + 32 * k;
+            v[j][k] = (i < n && 4 * c < D) ? o[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kMergeRound; ++j)
+#pragma unroll
+          for (int k = 0; k < kMergeMaxPerLane / 4; ++k) {
+            acc[k].x = fmaf(v[j][k].x, w[j], acc[k].x);
+            acc[k].y = fmaf(v[j][k].y, w[j], acc[k].y);
+            acc[k].z = fmaf(v[j][k].z, w[j], acc[k].z);
+            acc[k].w = fmaf(v[j][k].w, w[j], acc[k].w);
+          }
+      }
+#pragma unroll
+      for (int k = 0; k < kMergeMaxPerLane / 4; ++k) {
+        const uint32_t c = lane + 32 * k;
+        if (4 * c < D)
+          *reinterpret_cast<uint2 *>(out + h * D + 4 * c) =
+              make_uint2(pack_half2(acc[k].x * inv, acc[k].y * inv),
+                         pack_half2(acc[k].z * inv, acc[k].w * inv));
+      }
+    } else {
+      float acc[kMergeMaxPerLane];
+#pragma unroll
+      for (int k = 0; k < kMergeMaxPerLane; ++k)
+        acc[k] = 0.f;
 #pragma unroll 2
-    for (uint32_t i = 0; i < n; ++i) {
-      const float *r = record(i);
-      const float w = fast_exp2(r[h] - top);
-      const float *o = r + 2 * G + h * D;
+      for (uint32_t i = 0; i < n; ++i) {
+        const float w = weight(i);
+        const float *o = record(i) + 2 * G + h * D;
+#pragma unroll
+        for (int k = 0; k < kMergeMaxPerLane; ++k) {
+          const uint32_t d = lane + 32 * k;
+          if (d < D)
+            acc[k] = fmaf(o[d], w, acc[k]);
+        }
+      }
 #pragma unroll
       for (int k = 0; k < kMergeMaxPerLane; ++k) {
         const uint32_t d = lane + 32 * k;
         if (d < D)
-          acc[k] = fmaf(o[d], w, acc[k]);
+          out[h * D + d] = __float2half_rn(acc[k] * inv);
       }
-    }
-    const float inv = 1.f / sum;
-#pragma unroll
-    for (int k = 0; k < kMergeMaxPerLane; ++k) {
-      const uint32_t d = lane + 32 * k;
-      if (d < D)
-        out[h * D + d] = __float2half_rn(acc[k] * inv);
     }
   }
 }

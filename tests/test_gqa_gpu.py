@@ -94,6 +94,8 @@ def test_prefill_matches_dense_oracle(batch, tokens, past, hq, hkv, d):
     (2, 40, 16, 8, 64),        # CTA workers with per-warp pipelines
     (2, 50, 4, 2, 12),         # odd head_dim (CUDA-core path)
     (2, 20, 24, 2, 64),        # group of 12 (CUDA-core path)
+    (2, 90, 6, 2, 64),         # group of 3: the merge's scalar path
+    (4, 8320, 16, 4, 256),     # C5 decode shape: over 32 partial records per sequence
 ])
 def test_decode_matches_oracles(batch, past, hq, hkv, d):
     q, k, v = _inputs.gqa_case(batch, 1, past, hq, hkv, d, capacity=past + 5, seed=7 + past)
