@@ -40,6 +40,8 @@ def check(case, got_out, got_state):
 
 @pytest.mark.parametrize("batch,tokens,hk,dk,hv,dv,std", [
     (16, 1, 16, 128, 32, 128, 0.02),  # the recurrent-step config (C4), fewer sequences
+    (16, 3, 16, 128, 32, 128, 0.02),  # 32-column items, four per CTA, a few tokens
+    (8, 2, 8, 64, 32, 128, 0.02),     # the same with dk 64, two items per CTA
     (20, 1, 16, 128, 32, 128, 0.02),  # enough (sequence, head) pairs for 128-column CTAs
     (24, 3, 8, 64, 32, 128, 0.02),    # the same, dk 64, a few tokens
     (3, 1, 16, 128, 32, 128, 0.0),
