@@ -482,6 +482,34 @@ def time_op(torch, fn, dist, reps=10, warmup=3):
     return dist.max(statistics.median(t)), dist.max(t[0])
 
 
+def time_graph(torch, fn, dist, reps=50):
+    """Device time per call (ms, max over ranks) of fn captured once into a CUDA graph
+    and replayed `reps` times back to back between two events: the GPU-side cost of a
+    launch-bound call, without the host's per-call work."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()  # argument checks and one-time set-up outside the capture
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = dist.max(a.elapsed_time(b) / reps)
+    del graph
+    return ms
+
+
 def run_secondary(torch, ops, device, peaks, dist):
     """The other kernels of the path on their benchmark configs (CUDA events, median,
     max over ranks).  Every rank runs the whole config on its own GPU, so with N GPUs
@@ -496,12 +524,16 @@ def run_secondary(torch, ops, device, peaks, dist):
     vc = torch.randn(1, 128, 4, 256, generator=g, device=device).half()
     out = torch.empty_like(q)
     med, best = time_op(torch, lambda: ops.gqa_prefill(q, kc, vc, 0, out=out), dist)
+    graph_ms = time_graph(torch, lambda: ops.gqa_prefill(q, kc, vc, 0, out=out), dist)
     macs = step_bytes([1], 128, 0, 128, 1, query_heads=16, kv_heads=4, head_dim=256)["CausalGqa"][1]
     tf = 2 * macs / (med / 1e3) / 1e12
+    tf_graph = 2 * macs / (graph_ms / 1e3) / 1e12
     res.append({"workload": "C1 GQA prefill B=1 T=128 past 0 (gqaFlashAttention)"
                             + (f", {N} replicas" if N > 1 else ""),
                 "ms": round(med, 4), "value": round(tf * N, 3), "unit": "TFLOP/s",
-                "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4)})
+                "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4),
+                # Launch-bound: the same call captured in a CUDA graph and replayed.
+                "graph_replay_ms": round(graph_ms, 4), "graph_replay_value": round(tf_graph * N, 3)})
     del q, kc, vc, out
     # The GQA prefill at one C5 layer's shape: B=16 (per GPU), T=8192, past 0.
     # Each launch is ~9 ms and the loop runs under the power cap, so the

@@ -329,14 +329,16 @@ int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *
   const uint32_t rows = p.past + p.tokens;
   const uint64_t D = kD;
   CUtensorMap mq, mk, mv;
-  // caches [batch][rows][Hkv][D] at sequence stride cache_stride: K boxes are
-  // 64 dims x 1 head x 128 keys, V boxes 64 dims x 1 head x 32 keys.
+  const bool pairs = prefill_on_pairs();
+  // caches [batch][rows][Hkv][D] at sequence stride cache_stride.  Single
+  // CTAs stage K boxes of 64 dims x 1 head x 128 keys and V boxes of 32 keys;
+  // each CTA of a pair stages K boxes of 64 keys and V boxes of 128 keys.
   {
     const uint64_t seq_bytes = batch > 1 ? uint64_t(cache_stride) * 2 : uint64_t(rows) * p.kvHeads * D * 2;
     const uint64_t dims[4] = {D, p.kvHeads, rows, batch};
     const uint64_t strides[3] = {D * 2, uint64_t(p.kvHeads) * D * 2, seq_bytes};
-    const uint32_t kbox[4] = {64, 1, uint32_t(kKeys), 1};
-    const uint32_t vbox[4] = {64, 1, uint32_t(kVKeys), 1};
+    const uint32_t kbox[4] = {64, 1, uint32_t(pairs ? prefill_tc2::kHalfKeys : kKeys), 1};
+    const uint32_t vbox[4] = {64, 1, uint32_t(pairs ? prefill_tc2::kKeys : kVKeys), 1};
     if (int s = encode_map_4d(&mk, k, dims, strides, kbox))
       return s;
     if (int s = encode_map_4d(&mv, v, dims, strides, vbox))
@@ -362,18 +364,7 @@ int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *
   a.tok_per_tile = kRows / G;
   a.tiles_per_head = (p.tokens + a.tok_per_tile - 1) / a.tok_per_tile;
   a.scale_log2 = kLog2e / std::sqrt(float(kD));
-  if (prefill_on_pairs()) {
-    // CTA pairs: each CTA stages K boxes of 64 keys x 64 dims and V boxes
-    // of 128 keys x 64 dims.
-    const uint64_t seq_bytes = batch > 1 ? uint64_t(cache_stride) * 2 : uint64_t(rows) * p.kvHeads * D * 2;
-    const uint64_t dims[4] = {D, p.kvHeads, rows, batch};
-    const uint64_t strides[3] = {D * 2, uint64_t(p.kvHeads) * D * 2, seq_bytes};
-    const uint32_t kbox[4] = {64, 1, uint32_t(prefill_tc2::kHalfKeys), 1};
-    const uint32_t vbox[4] = {64, 1, uint32_t(prefill_tc2::kKeys), 1};
-    if (int s = encode_map_4d(&mk, k, dims, strides, kbox))
-      return s;
-    if (int s = encode_map_4d(&mv, v, dims, strides, vbox))
-      return s;
+  if (pairs) {
     a.tiles_per_head += a.tiles_per_head & 1u;
     auto kernel = prefill_tc2::gqa_prefill_pair;
     if (int s = allow_smem(reinterpret_cast<const void *>(kernel), prefill_tc2::Smem::alloc, dev))
