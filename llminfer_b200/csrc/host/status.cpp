@@ -10,7 +10,6 @@ namespace llmi {
 namespace {
 thread_local std::string g_message;
 
-constexpr int kMaxDevices = 64;
 std::mutex g_info_mutex;
 DeviceInfo g_info[kMaxDevices];
 }  // namespace

@@ -18,6 +18,9 @@ const char *last_error();
 // LLMI_OK for cudaSuccess, else LLMI_CUDA_ERROR with "<what>: <cuda message>".
 int check_cuda(cudaError_t error, const char *what);
 
+// Devices the library serves (current_device rejects higher indices).
+constexpr int kMaxDevices = 64;
+
 // Device attributes of the current device, cached per device.
 struct DeviceInfo {
   int device = -1;

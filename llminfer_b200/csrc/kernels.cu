@@ -915,6 +915,36 @@ extern "C" int llmi_cuda_delta_gates(const llmi_row_params *p, const uint16_t *a
   return launched("deltaGates");
 }
 
+namespace {
+
+// Fills the SiLU table (producers::g_silu_half) once per device before the
+// first kernel that reads it.  The fill is waited for on the host, so every
+// later call sees it whatever its stream; for that reason the first such call
+// on a device cannot run under stream capture.
+int ensure_silu_table(cudaStream_t s, const DeviceInfo &dev) {
+  static std::mutex mutex;
+  static bool ready[kMaxDevices] = {};
+  std::lock_guard<std::mutex> lock(mutex);
+  if (ready[dev.device])
+    return LLMI_OK;
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (int e = check_cuda(cudaStreamIsCapturing(s, &capture), "cudaStreamIsCapturing"))
+    return e;
+  if (capture != cudaStreamCaptureStatusNone)
+    return fail(LLMI_UNSUPPORTED,
+                "deltaPrepare: the first call on a device fills the SiLU table and cannot be "
+                "captured into a graph; make one call before capturing");
+  producers::silu_table_init<<<256, 256, 0, s>>>();
+  if (int e = launched("SiLU table"))
+    return e;
+  if (int e = check_cuda(cudaStreamSynchronize(s), "SiLU table"))
+    return e;
+  ready[dev.device] = true;
+  return LLMI_OK;
+}
+
+}  // namespace
+
 extern "C" int llmi_cuda_delta_prepare(const llmi_delta_prep_params *p, unsigned batch,
                                        const uint16_t *qkv, size_t qkv_stride,
                                        const uint16_t *conv_weight, uint16_t *history,
@@ -950,6 +980,11 @@ extern "C" int llmi_cuda_delta_prepare(const llmi_delta_prep_params *p, unsigned
                      aligned16(qkv) && aligned16(conv_weight) && aligned16(q) && aligned16(k) &&
                      aligned16(v) && (batch == 1 || qkv_stride % 8 == 0) && batch <= 65535;
   if (tiled) {
+    DeviceInfo dev;
+    if (int e = current_device(dev))
+      return e;
+    if (int e = ensure_silu_table(s, dev))
+      return e;
     const dim3 grid((p->tokens + producers::kPrepTokens - 1) / producers::kPrepTokens,
                     (heads + 7) / 8, batch);
     producers::delta_prepare_tiled<<<grid, 256, 0, s>>>(a);

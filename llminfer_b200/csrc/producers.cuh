@@ -33,6 +33,26 @@ __device__ __forceinline__ float stable_softplus(float x) {
 }
 __device__ __forceinline__ float round_half(float x) { return __half2float(__float2half_rn(x)); }
 
+// half(silu(half(x))) for every fp16 value of half(x): the conv's SiLU
+// epilogue takes an fp16 input and rounds its output to fp16, so it is a
+// function of 65536 inputs.  The table is filled once per device by
+// silu_table_init from the same silu() as above (so a lookup equals the
+// computed value bit for bit) and replaces about 25 instructions per element
+// (expf, a correctly rounded reciprocal, two conversions) by one cached load.
+__device__ __half g_silu_half[65536];
+
+__global__ void silu_table_init() {
+  const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < 65536u)
+    g_silu_half[i] =
+        __float2half_rn(silu(__half2float(__ushort_as_half(static_cast<unsigned short>(i)))));
+}
+
+__device__ __forceinline__ float silu_half(float acc) {
+  const unsigned short bits = __half_as_ushort(__float2half_rn(acc));
+  return __half2float(__ldg(&g_silu_half[bits]));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1)
@@ -337,7 +357,8 @@ __global__ void __launch_bounds__(256) delta_prepare(const PrepArgs a) {
 // 4l..4l+3 of the head: their 4 x 4 taps in registers, and a sliding window
 // of the last three input rows (8-byte loads), so every input row is read
 // once per tile and every weight once per warp.  The tap sums keep the
-// reference's order.  Grid (token tiles, ceil(heads / 8), batch).
+// reference's order; SiLU comes from the per-device fp16 table (silu_half).
+// Grid (token tiles, ceil(heads / 8), batch).
 constexpr int kPrepTokens = 32;
 __global__ void __launch_bounds__(256, 4) delta_prepare_tiled(const PrepArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -417,7 +438,7 @@ __global__ void __launch_bounds__(256, 4) delta_prepare_tiled(const PrepArgs a) 
       acc = fmaf(x3[e], w[e][0], acc);
       acc = fmaf(x2[e], w[e][1], acc);
       acc = fmaf(x1[e], w[e][2], acc);
-      y[e] = round_half(silu(round_half(acc)));
+      y[e] = silu_half(acc);
       sum = fmaf(y[e], y[e], sum);
     }
     const size_t tok = size_t(seq) * a.conv.tokens + t;

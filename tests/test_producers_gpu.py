@@ -98,9 +98,12 @@ def test_causal_conv(batch, tokens, channels, k, silu):
     np.testing.assert_array_equal(h.cpu().numpy().view(np.uint16), exp_hist.view(np.uint16))
 
 
-@pytest.mark.parametrize("batch,tokens", [(2, 1), (1, 3), (2, 70)])
-def test_delta_prepare(batch, tokens):
-    hk, dk, hv, dv, kern = 4, 128, 8, 128, 4
+@pytest.mark.parametrize("batch,tokens,hk,hv", [
+    (2, 1, 4, 8), (1, 3, 4, 8), (2, 70, 4, 8),
+    (2, 40, 2, 5),   # 9 heads: the second group of 8 holds one
+])
+def test_delta_prepare(batch, tokens, hk, hv):
+    dk, dv, kern = 128, 128, 4
     width = 2 * hk * dk + hv * dv
     qkv = _inputs.half_normal(50 + tokens, 1, (batch, tokens, width))
     w = _inputs.normal(50 + tokens, 2, (width, kern), 0.5).astype(np.float16)
@@ -112,6 +115,21 @@ def test_delta_prepare(batch, tokens):
     np.testing.assert_allclose(k.cpu().numpy(), ek, rtol=4e-6, atol=1e-7)
     check_f16(v, ev)
     np.testing.assert_array_equal(h.cpu().numpy().view(np.uint16), eh.view(np.uint16))
+
+
+def test_delta_prepare_silu_table_matches_computed_silu():
+    # The tiled deltaPrepare takes half(silu(half(acc))) from a per-device
+    # fp16 table; the element-wise causalConv computes it.  The v channels of
+    # both must agree bit for bit over a wide range of conv outputs.
+    batch, tokens, hk, dk, hv, dv, kern = 2, 50, 2, 128, 4, 128, 4
+    width = 2 * hk * dk + hv * dv
+    qkv = (_inputs.half_normal(80, 1, (batch, tokens, width)).astype(np.float32) * 8).astype(np.float16)
+    w = _inputs.normal(80, 2, (width, kern), 1.0).astype(np.float16)
+    hist = _inputs.half_normal(80, 3, (batch, width, kern - 1))
+    _, _, v = ops.delta_prepare(dev(qkv), dev(w), dev(hist), hk, dk, hv, dv)
+    conv = ops.causal_conv(dev(qkv), dev(w), dev(hist), True)
+    np.testing.assert_array_equal(v.cpu().numpy().view(np.uint16),
+                                  conv[..., 2 * hk * dk:].cpu().numpy().view(np.uint16))
 
 
 def test_delta_prepare_feeds_delta_update():
