@@ -298,7 +298,12 @@ typedef struct {
   void *out;
 } llmi_layer_io;
 
-enum { LLMI_STATE_KEYS = 0, LLMI_STATE_VALUES = 1, LLMI_STATE_RECURRENT = 2 };
+enum {
+  LLMI_STATE_KEYS = 0,
+  LLMI_STATE_VALUES = 1,
+  LLMI_STATE_RECURRENT = 2,
+  LLMI_STATE_CONV_HISTORY = 3 /* DeltaNet layers, after set_producers */
+};
 
 /* Allocates and zeroes the states (MetalExecutor::initialize,
  * MetalExecutor.mm:56-94) on the current device; `stream` is borrowed. */
@@ -360,6 +365,53 @@ int llmi_cuda_session_read_state(llmi_session *session, unsigned layer,
 int llmi_cuda_session_write_state(llmi_session *session, unsigned layer,
                                   unsigned which, const void *src,
                                   size_t bytes);
+
+/* Producers of the layers' operands inside the session: the KV-cache
+ * producers and the DeltaNet input producers run ahead of the attention
+ * ops.  Settings of Qwen3.5's q/k RmsNorm + PartialRoPE
+ * (Qwen35ModelBuilder.cpp:187-191) and of the DeltaNet block's conv, L2Norm
+ * and gates (Qwen35ModelBuilder.cpp:146-157). */
+typedef struct {
+  unsigned rotaryDim;  /* even, <= headDim and <= 256 */
+  float ropeTheta, normEpsilon;
+  unsigned convKernel; /* 1..8 */
+  float l2Epsilon;
+} llmi_producer_config;
+
+/* Enables llmi_cuda_session_step_projections: keeps the settings and
+ * allocates one ConvHistory state per DeltaNet layer ([batch][W][convKernel-1]
+ * fp16, W = 2*keyHeads*keyDim + valueHeads*valueDim), zeroed now and by every
+ * reset.  Once per session. */
+int llmi_cuda_session_set_producers(llmi_session *session,
+                                    const llmi_producer_config *config);
+
+/* One layer's projection outputs and weights (device pointers, dense,
+ * batch-major), the inputs of llmi_cuda_session_step_projections:
+ *   GQA:      qg f16 [B][T][Hq][2D] (q_proj's [q | gate] rows; q is read,
+ *             gate is left to the caller), k, v f16 [B][T][Hkv][D],
+ *             qNorm, kNorm f32 [D] (RmsNorm weights, applied as 1 + w),
+ *             out f16 [B][T][Hq][D]
+ *   DeltaNet: qkv f16 [B][T][W], a, b f16 [B][T][Hv], convWeight f16 [W][K],
+ *             aLog, dtBias f32 [Hv], out f16 [B][T][Hv*dv] */
+typedef struct {
+  const void *qg, *k, *v;
+  const float *qNorm, *kNorm;
+  const void *qkv, *a, *b, *convWeight;
+  const float *aLog, *dtBias;
+  void *out;
+} llmi_layer_projections;
+
+/* llmi_cuda_session_step from the projections: per GQA layer normRope of q
+ * (into session scratch), normRope of k straight into the key cache at row
+ * past (the keys' cacheAppend), cacheAppend of v, then the attention; per
+ * DeltaNet layer deltaPrepare (conv + SiLU over the layer's ConvHistory, the
+ * slices, the q/k L2Norms) and deltaGates into session scratch, then
+ * graphDeltaUpdate.  Same checks, wait and failure rules as session_step;
+ * the scratch grows to the largest step seen (so the first step of a size
+ * may allocate).  The traced plan lists the producer dispatches too. */
+int llmi_cuda_session_step_projections(llmi_session *session, unsigned tokens,
+                                       const llmi_layer_projections *io,
+                                       int trace_plan);
 
 /* The last traced step's dispatches as JSON lines
  * {"op_index":i,"kernel":"...","layer":l} — the records llmi-run --plan prints

@@ -28,6 +28,7 @@ LAYER_GQA = 1
 STATE_KEYS = 0
 STATE_VALUES = 1
 STATE_RECURRENT = 2
+STATE_CONV_HISTORY = 3
 
 
 class CacheParams(ctypes.Structure):
@@ -88,6 +89,18 @@ class LayerIO(ctypes.Structure):
                 ("beta", c_void_p), ("decay", c_void_p), ("out", c_void_p)]
 
 
+class ProducerConfig(ctypes.Structure):
+    _fields_ = [("rotaryDim", c_uint), ("ropeTheta", c_float), ("normEpsilon", c_float),
+                ("convKernel", c_uint), ("l2Epsilon", c_float)]
+
+
+class LayerProjections(ctypes.Structure):
+    _fields_ = [("qg", c_void_p), ("k", c_void_p), ("v", c_void_p),
+                ("qNorm", c_void_p), ("kNorm", c_void_p),
+                ("qkv", c_void_p), ("a", c_void_p), ("b", c_void_p), ("convWeight", c_void_p),
+                ("aLog", c_void_p), ("dtBias", c_void_p), ("out", c_void_p)]
+
+
 # (name, restype, argtypes) of every exported entry point, in header order.
 SIGNATURES = [
     ("llmi_cuda_last_error", c_char_p, []),
@@ -134,6 +147,9 @@ SIGNATURES = [
      [c_void_p, c_uint, c_uint, POINTER(c_void_p), POINTER(c_size_t)]),
     ("llmi_cuda_session_read_state", c_int, [c_void_p, c_uint, c_uint, c_void_p, c_size_t]),
     ("llmi_cuda_session_write_state", c_int, [c_void_p, c_uint, c_uint, c_void_p, c_size_t]),
+    ("llmi_cuda_session_set_producers", c_int, [c_void_p, POINTER(ProducerConfig)]),
+    ("llmi_cuda_session_step_projections", c_int,
+     [c_void_p, c_uint, POINTER(LayerProjections), c_int]),
     ("llmi_cuda_session_plan", c_size_t, [c_void_p, c_char_p, c_size_t]),
     ("llmi_cuda_describe_step", c_size_t,
      [POINTER(StackConfig), c_uint, c_uint64, c_char_p, c_size_t, POINTER(c_int)]),

@@ -42,14 +42,26 @@ struct llmi_session {
   std::string plan;
   std::vector<cudaEvent_t> layerEvents;  // borrowed; recorded after each layer
   unsigned injectFaultUs = 0;             // > 0: the next step also runs the wait self-test
+  // Producers (llmi_cuda_session_set_producers): their settings, the
+  // ConvHistory state of each DeltaNet layer and a scratch arena for the
+  // producers' outputs, shared by the layers (they run in order on one
+  // stream).
+  bool producers = false;
+  llmi_producer_config prod{};
+  std::vector<void *> convHistory;
+  size_t historyBytes = 0;
+  void *scratch = nullptr;
+  size_t scratchBytes = 0;
 
   ~llmi_session() {
-    for (auto *list : {&keys, &values, &recurrent})
+    for (auto *list : {&keys, &values, &recurrent, &convHistory})
       for (void *p : *list)
         if (p)
           cudaFree(p);
     if (workspace)
       cudaFree(workspace);
+    if (scratch)
+      cudaFree(scratch);
   }
 };
 
@@ -67,6 +79,10 @@ int zero_states(llmi_session &s) {
     if (s.recurrent[l])
       if (int e = check_cuda(cudaMemsetAsync(s.recurrent[l], 0, s.recurrentBytes, s.stream),
                              "zero recurrent state"))
+        return e;
+    if (l < s.convHistory.size() && s.convHistory[l])
+      if (int e = check_cuda(cudaMemsetAsync(s.convHistory[l], 0, s.historyBytes, s.stream),
+                             "zero conv history"))
         return e;
   }
   return check_cuda(cudaStreamSynchronize(s.stream), "zero states");
@@ -100,18 +116,80 @@ int check_io(const llmi_session &s, const llmi_layer_io *io) {
   return LLMI_OK;
 }
 
+int check_projections(const llmi_session &s, const llmi_layer_projections *io) {
+  if (!s.producers)
+    return fail(LLMI_INVALID_ARGUMENT,
+                "step_projections: the session has no producer settings (set_producers)");
+  if (!io)
+    return fail(LLMI_INVALID_ARGUMENT, "step_projections: null layer operand table");
+  for (size_t l = 0; l < s.config.kinds.size(); ++l) {
+    const llmi_layer_projections &x = io[l];
+    const bool ok = s.config.kinds[l] == LLMI_LAYER_GQA
+                        ? x.qg && x.k && x.v && x.qNorm && x.kNorm && x.out
+                        : x.qkv && x.a && x.b && x.convWeight && x.aLog && x.dtBias && x.out;
+    if (!ok)
+      return fail(LLMI_INVALID_ARGUMENT, "step_projections: layer %zu is missing an operand", l);
+  }
+  return LLMI_OK;
+}
+
+// Offsets of the producers' outputs in the scratch arena for a step of
+// `tokens` (256-byte aligned): GQA layers use q, DeltaNet layers q..decay.
+struct ScratchLayout {
+  size_t q = 0, k = 0, v = 0, beta = 0, decay = 0, bytes = 0;
+  ScratchLayout(const StackConfig &c, unsigned tokens) {
+    const size_t rows = size_t(c.batch) * tokens;
+    auto up = [](size_t n) { return (n + 255) & ~size_t(255); };
+    const size_t gqa = up(rows * c.queryHeads * c.headDim * 2);
+    k = up(rows * c.keyHeads * c.keyDim * 4);
+    v = 2 * k;
+    beta = v + up(rows * c.valueHeads * c.valueDim * 2);
+    decay = beta + up(rows * c.valueHeads * 4);
+    const size_t delta = decay + up(rows * c.valueHeads * 4);
+    bytes = std::max(c.hasGqa() ? gqa : 0, c.hasDelta() ? delta : 0);
+  }
+};
+
+int ensure_scratch(llmi_session &s, size_t bytes) {
+  if (bytes <= s.scratchBytes)
+    return LLMI_OK;
+  if (s.scratch) {
+    if (int e = check_cuda(cudaStreamSynchronize(s.stream), "scratch resize"))
+      return e;
+    cudaFree(s.scratch);
+    s.scratch = nullptr;
+    s.scratchBytes = 0;
+  }
+  if (int e = check_cuda(cudaMalloc(&s.scratch, bytes), "allocate producer scratch"))
+    return e;
+  s.scratchBytes = bytes;
+  return LLMI_OK;
+}
+
 // Lowers and launches one step.  `launchedAny` reports whether any kernel
-// may have been enqueued (the reference's "submitted").
+// may have been enqueued (the reference's "submitted").  With `proj`, each
+// layer's producers run first (into the scratch arena, and for keys straight
+// into the cache) and the layer's attention operands are their outputs.
 int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool trace,
-             bool &launchedAny) {
+             bool &launchedAny, const llmi_layer_projections *proj = nullptr) {
   launchedAny = false;
   AttentionGraph graph;
   if (int e = AttentionGraph::build(s.config, {tokens, s.past, s.config.capacity}, graph))
     return e;
-  if (int e = check_io(s, io))
-    return e;
   const StackConfig &c = s.config;
   const unsigned B = c.batch;
+  std::vector<llmi_layer_io> produced;
+  ScratchLayout layout(c, tokens);
+  if (proj) {
+    if (int e = check_projections(s, proj))
+      return e;
+    if (int e = ensure_scratch(s, layout.bytes))
+      return e;
+    produced.assign(c.kinds.size(), llmi_layer_io{});
+    io = produced.data();
+  } else if (int e = check_io(s, io)) {
+    return e;
+  }
   if (tokens == 1 && c.hasGqa()) {
     llmi_gqa_params g{1, c.queryHeads, c.kvHeads, c.headDim, unsigned(s.past)};
     const size_t need = llmi_cuda_gqa_decode_workspace(&g, B);
@@ -124,11 +202,83 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
   const auto dispatches = lower(graph);
   size_t next = 0;  // first dispatch of the current op
   const auto &ops = graph.ops();
+  auto record = [&](size_t opIndex, const char *kernel, uint32_t layer) {
+    char line[160];
+    std::snprintf(line, sizeof line, "{\"op_index\":%zu,\"kernel\":\"%s\",\"layer\":%u}\n",
+                  opIndex, kernel, layer);
+    s.plan += line;
+  };
+  // The producers of layer l from its projections (step_projections).
+  auto produce = [&](uint32_t l, size_t opIndex) -> int {
+    const llmi_layer_projections &p = proj[l];
+    llmi_layer_io &x = produced[l];
+    uint8_t *base = static_cast<uint8_t *>(s.scratch);
+    x.out = p.out;
+    launchedAny = true;
+    if (c.kinds[l] == LLMI_LAYER_GQA) {
+      uint16_t *q = reinterpret_cast<uint16_t *>(base + layout.q);
+      const llmi_rope_params rq{tokens, c.queryHeads, c.headDim, s.prod.rotaryDim,
+                                2 * c.headDim, unsigned(s.past), 0u, s.prod.normEpsilon,
+                                s.prod.ropeTheta};
+      if (int e = llmi_cuda_norm_rope(&rq, B, static_cast<const uint16_t *>(p.qg),
+                                      size_t(tokens) * c.queryHeads * 2 * c.headDim, p.qNorm, q,
+                                      size_t(tokens) * c.queryHeads * c.headDim, s.stream))
+        return e;
+      // Keys go straight into the cache at row past: the keys' cacheAppend.
+      const llmi_rope_params rk{tokens, c.kvHeads, c.headDim, s.prod.rotaryDim, c.headDim,
+                                unsigned(s.past), unsigned(s.past), s.prod.normEpsilon,
+                                s.prod.ropeTheta};
+      if (int e = llmi_cuda_norm_rope(&rk, B, static_cast<const uint16_t *>(p.k),
+                                      size_t(tokens) * c.kvHeads * c.headDim, p.kNorm,
+                                      static_cast<uint16_t *>(s.keys[l]), cacheStride, s.stream))
+        return e;
+      x.q = q;
+      x.v = p.v;
+      if (trace) {
+        record(opIndex, "normRope", l);
+        record(opIndex, "normRope", l);
+      }
+    } else {
+      const unsigned W = 2 * c.keyHeads * c.keyDim + c.valueHeads * c.valueDim;
+      float *q = reinterpret_cast<float *>(base + layout.q);
+      float *k = reinterpret_cast<float *>(base + layout.k);
+      uint16_t *v = reinterpret_cast<uint16_t *>(base + layout.v);
+      float *beta = reinterpret_cast<float *>(base + layout.beta);
+      float *decay = reinterpret_cast<float *>(base + layout.decay);
+      const llmi_delta_prep_params dp{tokens, c.keyHeads, c.keyDim, c.valueHeads, c.valueDim,
+                                      W, s.prod.convKernel, s.prod.l2Epsilon};
+      if (int e = llmi_cuda_delta_prepare(&dp, B, static_cast<const uint16_t *>(p.qkv),
+                                          size_t(tokens) * W,
+                                          static_cast<const uint16_t *>(p.convWeight),
+                                          static_cast<uint16_t *>(s.convHistory[l]),
+                                          size_t(W) * (s.prod.convKernel - 1), q, k, v, s.stream))
+        return e;
+      const llmi_row_params rp{B * tokens, c.valueHeads, 0.f};
+      if (int e = llmi_cuda_delta_gates(&rp, static_cast<const uint16_t *>(p.a),
+                                        static_cast<const uint16_t *>(p.b), p.aLog, p.dtBias,
+                                        beta, decay, s.stream))
+        return e;
+      x.q = q;
+      x.k = k;
+      x.v = v;
+      x.beta = beta;
+      x.decay = decay;
+      if (trace) {
+        record(opIndex, "deltaPrepare", l);
+        record(opIndex, "deltaGates", l);
+      }
+    }
+    return LLMI_OK;
+  };
   for (size_t i = 0; i < ops.size(); ++i) {
     const Op &op = ops[i];
+    if (proj && (i == 0 || ops[i - 1].layer != op.layer))
+      if (int e = produce(op.layer, next < dispatches.size() ? dispatches[next].opIndex : i))
+        return e;
     const llmi_layer_io &x = io[op.layer];
     int e = LLMI_OK;
     size_t count = 1;
+    size_t skip = 0;  // leading dispatches of the op that the producers already did
     // One NVTX range per op (no-op unless a profiler is attached), named
     // like its first --plan dispatch.
     struct Range {
@@ -141,8 +291,12 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
       llmi_cache_params p{tokens * row, unsigned(s.past) * row};
       const size_t inStride = size_t(tokens) * row;
       launchedAny = true;
-      e = llmi_cuda_cache_append(&p, B, static_cast<const uint16_t *>(x.k), inStride,
-                                 static_cast<uint16_t *>(s.keys[op.layer]), cacheStride, s.stream);
+      if (proj)
+        skip = 1;  // normRope wrote the keys
+      else
+        e = llmi_cuda_cache_append(&p, B, static_cast<const uint16_t *>(x.k), inStride,
+                                   static_cast<uint16_t *>(s.keys[op.layer]), cacheStride,
+                                   s.stream);
       if (!e)
         e = llmi_cuda_cache_append(&p, B, static_cast<const uint16_t *>(x.v), inStride,
                                    static_cast<uint16_t *>(s.values[op.layer]), cacheStride,
@@ -186,12 +340,8 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
                               "record layer event"))
         return st;
     if (trace)
-      for (size_t d = next; d < next + count && d < dispatches.size(); ++d) {
-        char line[160];
-        std::snprintf(line, sizeof line, "{\"op_index\":%zu,\"kernel\":\"%s\",\"layer\":%u}\n",
-                      dispatches[d].opIndex, dispatches[d].kernel, dispatches[d].layer);
-        s.plan += line;
-      }
+      for (size_t d = next + skip; d < next + count && d < dispatches.size(); ++d)
+        record(dispatches[d].opIndex, dispatches[d].kernel, dispatches[d].layer);
     next += count;
   }
   if (s.injectFaultUs) {
@@ -279,8 +429,13 @@ extern "C" void llmi_cuda_session_close(llmi_session *session) {
   delete session;
 }
 
-extern "C" int llmi_cuda_session_step(llmi_session *s, unsigned tokens, const llmi_layer_io *io,
-                                      int trace_plan) {
+namespace {
+
+// session_step and session_step_projections: launch, wait, check the device
+// error word; past advances only on success, and a failure after launch
+// invalidates the session.
+int step_and_wait(llmi_session *s, unsigned tokens, const llmi_layer_io *io,
+                  const llmi_layer_projections *proj, int trace_plan) {
   clear_error();
   if (!s)
     return fail(LLMI_INVALID_ARGUMENT, "step: null session");
@@ -289,7 +444,7 @@ extern "C" int llmi_cuda_session_step(llmi_session *s, unsigned tokens, const ll
   if (trace_plan)
     s->plan.clear();
   bool launchedAny = false;
-  int e = run_step(*s, tokens, io, trace_plan != 0, launchedAny);
+  int e = run_step(*s, tokens, io, trace_plan != 0, launchedAny, proj);
   if (!e && launchedAny)
     e = llmi_cuda_poll_error(s->stream);
   if (e) {
@@ -297,6 +452,60 @@ extern "C" int llmi_cuda_session_step(llmi_session *s, unsigned tokens, const ll
     return e;
   }
   s->past += tokens;
+  return LLMI_OK;
+}
+
+}  // namespace
+
+extern "C" int llmi_cuda_session_step(llmi_session *s, unsigned tokens, const llmi_layer_io *io,
+                                      int trace_plan) {
+  return step_and_wait(s, tokens, io, nullptr, trace_plan);
+}
+
+extern "C" int llmi_cuda_session_step_projections(llmi_session *s, unsigned tokens,
+                                                  const llmi_layer_projections *io,
+                                                  int trace_plan) {
+  if (!io) {
+    clear_error();
+    return fail(LLMI_INVALID_ARGUMENT, "step_projections: null layer operand table");
+  }
+  return step_and_wait(s, tokens, nullptr, io, trace_plan);
+}
+
+extern "C" int llmi_cuda_session_set_producers(llmi_session *s, const llmi_producer_config *p) {
+  clear_error();
+  if (!s || !p)
+    return fail(LLMI_INVALID_ARGUMENT, "set_producers: null session or settings");
+  if (s->producers)
+    return fail(LLMI_INVALID_ARGUMENT, "set_producers: already set for this session");
+  const StackConfig &c = s->config;
+  if (c.hasGqa() && (p->rotaryDim % 2 || p->rotaryDim > c.headDim || p->rotaryDim > 256 ||
+                     c.headDim > 1024))
+    return fail(LLMI_UNSUPPORTED,
+                "set_producers: rotaryDim %u (even, <= headDim %u and <= 256; headDim <= 1024)",
+                p->rotaryDim, c.headDim);
+  if (c.hasDelta() && (p->convKernel < 2 || p->convKernel > 8 || c.keyDim > 256 ||
+                       c.valueDim > 256))
+    return fail(LLMI_UNSUPPORTED,
+                "set_producers: convKernel %u (2..8) with keyDim %u / valueDim %u (<= 256)",
+                p->convKernel, c.keyDim, c.valueDim);
+  const size_t W = 2 * size_t(c.keyHeads) * c.keyDim + size_t(c.valueHeads) * c.valueDim;
+  s->convHistory.assign(c.kinds.size(), nullptr);
+  s->historyBytes = size_t(c.batch) * W * (p->convKernel - 1) * 2;
+  for (size_t l = 0; l < c.kinds.size(); ++l) {
+    if (c.kinds[l] != LLMI_LAYER_DELTANET)
+      continue;
+    if (int e = check_cuda(cudaMalloc(&s->convHistory[l], s->historyBytes),
+                           "allocate conv history"))
+      return e;
+    if (int e = check_cuda(cudaMemsetAsync(s->convHistory[l], 0, s->historyBytes, s->stream),
+                           "zero conv history"))
+      return e;
+  }
+  if (int e = check_cuda(cudaStreamSynchronize(s->stream), "zero conv history"))
+    return e;
+  s->prod = *p;
+  s->producers = true;
   return LLMI_OK;
 }
 
@@ -391,6 +600,9 @@ extern "C" int llmi_cuda_session_state(llmi_session *s, unsigned layer, unsigned
   } else if (which == LLMI_STATE_RECURRENT) {
     p = s->recurrent[layer];
     n = s->recurrentBytes;
+  } else if (which == LLMI_STATE_CONV_HISTORY && layer < s->convHistory.size()) {
+    p = s->convHistory[layer];
+    n = s->historyBytes;
   }
   if (!p)
     return fail(LLMI_INVALID_ARGUMENT, "session_state: layer %u has no such state", layer);

@@ -235,6 +235,32 @@ class LayerTensors:
                            ptr(self.decay), ptr(self.out))
 
 
+@dataclass
+class LayerProjections:
+    """One layer's projection outputs and weights (see llmi_layer_projections in
+    llmi_cuda.h).  GQA layers: qg, k, v, q_norm, k_norm, out; DeltaNet layers: qkv,
+    a, b, conv_weight, a_log, dt_bias, out."""
+    out: torch.Tensor
+    qg: torch.Tensor | None = None
+    k: torch.Tensor | None = None
+    v: torch.Tensor | None = None
+    q_norm: torch.Tensor | None = None
+    k_norm: torch.Tensor | None = None
+    qkv: torch.Tensor | None = None
+    a: torch.Tensor | None = None
+    b: torch.Tensor | None = None
+    conv_weight: torch.Tensor | None = None
+    a_log: torch.Tensor | None = None
+    dt_bias: torch.Tensor | None = None
+
+    def to_abi(self) -> abi.LayerProjections:
+        ptr = lambda t: None if t is None else t.data_ptr()
+        return abi.LayerProjections(ptr(self.qg), ptr(self.k), ptr(self.v), ptr(self.q_norm),
+                                    ptr(self.k_norm), ptr(self.qkv), ptr(self.a), ptr(self.b),
+                                    ptr(self.conv_weight), ptr(self.a_log), ptr(self.dt_bias),
+                                    ptr(self.out))
+
+
 class AttentionSession:
     """The attention-stack session (llmi_cuda_session_*), a MetalSession for the attention ops."""
 
@@ -271,6 +297,23 @@ class AttentionSession:
     def step(self, tokens: int, layers, trace_plan: bool = False) -> None:
         self._sync_inputs()
         check(lib.llmi_cuda_session_step(self._handle, tokens, self._io(layers), int(trace_plan)))
+
+    def set_producers(self, rotary_dim: int = 64, rope_theta: float = 10_000_000.0,
+                      norm_epsilon: float = 1e-6, conv_kernel: int = 4,
+                      l2_epsilon: float = 1e-6) -> None:
+        """Enable step_projections (llmi_cuda_session_set_producers)."""
+        self._producers = abi.ProducerConfig(rotary_dim, rope_theta, norm_epsilon, conv_kernel,
+                                             l2_epsilon)
+        check(lib.llmi_cuda_session_set_producers(self._handle, ctypes.byref(self._producers)))
+
+    def step_projections(self, tokens: int, layers, trace_plan: bool = False) -> None:
+        """A step from the layers' projection outputs (a list of LayerProjections)."""
+        if len(layers) != len(self.kinds):
+            raise ValueError(f"{len(layers)} layer operand sets for {len(self.kinds)} layers")
+        self._sync_inputs()
+        table = (abi.LayerProjections * len(layers))(*[x.to_abi() for x in layers])
+        check(lib.llmi_cuda_session_step_projections(self._handle, tokens, table,
+                                                      int(trace_plan)))
 
     def operand_table(self, layers):
         """The C operand table (llmi_layer_io[]) of `layers`.  It holds raw device
@@ -328,6 +371,9 @@ class AttentionSession:
         s = self.shape
         if which == abi.STATE_RECURRENT:
             return (self.batch, s["value_heads"], s["key_dim"], s["value_dim"]), torch.float32
+        if which == abi.STATE_CONV_HISTORY:
+            width = 2 * s["key_heads"] * s["key_dim"] + s["value_heads"] * s["value_dim"]
+            return (self.batch, width, self._producers.convKernel - 1), torch.float16
         return (self.batch, self.capacity, s["kv_heads"], s["head_dim"]), torch.float16
 
     def read_state(self, layer: int, which: int) -> torch.Tensor:

@@ -135,3 +135,100 @@ def test_partition_invariance():
                                        atol=1e-5, rtol=1e-5)
     a.close()
     b.close()
+
+
+PRODUCER_KINDS = [abi.LAYER_DELTANET, abi.LAYER_GQA]
+
+
+def projection_inputs(batch, tokens, seed):
+    """Projection outputs and weights of one step for PRODUCER_KINDS."""
+    s = SHAPE
+    width = 2 * s["key_heads"] * s["key_dim"] + s["value_heads"] * s["value_dim"]
+    hv = s["value_heads"]
+    delta = dict(
+        qkv=dev(_inputs.half_normal(seed, 1, (batch, tokens, width))),
+        a=dev(_inputs.normal(seed, 2, (batch, tokens, hv), 2.0).astype(np.float16)),
+        b=dev(_inputs.normal(seed, 3, (batch, tokens, hv), 2.0).astype(np.float16)))
+    gqa = dict(
+        qg=dev(_inputs.half_normal(seed, 4, (batch, tokens, s["query_heads"], 2 * s["head_dim"]))),
+        k=dev(_inputs.half_normal(seed, 5, (batch, tokens, s["kv_heads"], s["head_dim"]))),
+        v=dev(_inputs.half_normal(seed, 6, (batch, tokens, s["kv_heads"], s["head_dim"]))))
+    return delta, gqa
+
+
+def test_step_projections_equals_the_composed_producers_and_ops():
+    # The session's producer path runs the same kernels as composing the ops
+    # by hand (norm_rope into the cache, cache_append of v, the attention;
+    # delta_prepare over the conv history, delta_gates, delta_update), so
+    # outputs and every state agree bit for bit: a prefill, a decode step and
+    # a short multi-token step.
+    s = SHAPE
+    batch, capacity, rot, theta, conv = 2, 64, 64, 10_000_000.0, 4
+    width = 2 * s["key_heads"] * s["key_dim"] + s["value_heads"] * s["value_dim"]
+    hv = s["value_heads"]
+    conv_w = dev(_inputs.normal(90, 1, (width, conv), 0.5).astype(np.float16))
+    a_log = dev(_inputs.normal(90, 2, (hv,), 0.5))
+    dt_bias = dev(_inputs.normal(90, 3, (hv,), 0.5))
+    q_norm = dev(_inputs.normal(90, 4, (s["head_dim"],), 0.1))
+    k_norm = dev(_inputs.normal(90, 5, (s["head_dim"],), 0.1))
+
+    session = ops.AttentionSession(PRODUCER_KINDS, batch, capacity, **SHAPE)
+    session.set_producers(rotary_dim=rot, rope_theta=theta, conv_kernel=conv)
+    # The composed reference: its own caches, state and conv history.
+    keys = torch.zeros(batch, capacity, s["kv_heads"], s["head_dim"], dtype=torch.float16,
+                       device="cuda")
+    values = torch.zeros_like(keys)
+    state = torch.zeros(batch, hv, s["key_dim"], s["value_dim"], device="cuda")
+    hist = torch.zeros(batch, width, conv - 1, dtype=torch.float16, device="cuda")
+    past = 0
+    for step, tokens in enumerate([40, 1, 3]):
+        delta, gqa = projection_inputs(batch, tokens, 91 + step)
+        out_d = torch.full((batch, tokens, hv * s["value_dim"]), float("nan"),
+                           dtype=torch.float16, device="cuda")
+        out_g = torch.full((batch, tokens, s["query_heads"], s["head_dim"]), float("nan"),
+                           dtype=torch.float16, device="cuda")
+        layers = [ops.LayerProjections(out=out_d, conv_weight=conv_w, a_log=a_log,
+                                       dt_bias=dt_bias, **delta),
+                  ops.LayerProjections(out=out_g, q_norm=q_norm, k_norm=k_norm, **gqa)]
+        session.step_projections(tokens, layers, trace_plan=True)
+        torch.cuda.synchronize()
+
+        q, k, v = ops.delta_prepare(delta["qkv"], conv_w, hist, s["key_heads"], s["key_dim"],
+                                    hv, s["value_dim"])
+        beta, decay = ops.delta_gates(delta["a"], delta["b"], a_log, dt_bias)
+        ref_d = ops.delta_update(q, k, v, beta, decay, state)
+        qr = ops.norm_rope(gqa["qg"], q_norm, past, rot, theta, head_dim=s["head_dim"])
+        ops.norm_rope(gqa["k"], k_norm, past, rot, theta, out=keys, output_start=past)
+        ops.cache_append(gqa["v"], values, past)
+        ref_g = (ops.gqa_prefill(qr, keys, values, past) if tokens > 1
+                 else ops.gqa_decode(qr, keys, values, past))
+        torch.cuda.synchronize()
+        past += tokens
+
+        assert torch.equal(out_d, ref_d), step
+        assert torch.equal(out_g, ref_g), step
+        assert session.past == past
+        assert torch.equal(session.read_state(0, abi.STATE_RECURRENT), state)
+        assert torch.equal(session.read_state(0, abi.STATE_CONV_HISTORY), hist)
+        assert torch.equal(session.read_state(1, abi.STATE_KEYS), keys)
+        assert torch.equal(session.read_state(1, abi.STATE_VALUES), values)
+        kernels = [d["kernel"] for d in session.plan()]
+        assert kernels[:3] == ["deltaPrepare", "deltaGates", "graphDeltaUpdate"]
+        assert kernels[3:6] == ["normRope", "normRope", "cacheAppend"]
+        assert kernels[6:] == (["gqaFlashAttention"] if tokens > 1 else ["gqaScores", "gqaSoftmax"])
+
+    session.reset()
+    assert not session.read_state(0, abi.STATE_CONV_HISTORY).any()
+    session.close()
+
+
+def test_step_projections_needs_producer_settings():
+    session = ops.AttentionSession(PRODUCER_KINDS, 1, 8, **SHAPE)
+    delta, gqa = projection_inputs(1, 2, 7)
+    out = torch.empty(1, 2, 512, dtype=torch.float16, device="cuda")
+    layers = [ops.LayerProjections(out=out, **delta), ops.LayerProjections(out=out, **gqa)]
+    with pytest.raises(abi.LlmiError) as err:
+        session.step_projections(2, layers)
+    assert err.value.status == abi.LLMI_INVALID_ARGUMENT
+    assert session.past == 0 and not session.invalid
+    session.close()
