@@ -232,3 +232,19 @@ def test_step_projections_needs_producer_settings():
     assert err.value.status == abi.LLMI_INVALID_ARGUMENT
     assert session.past == 0 and not session.invalid
     session.close()
+
+
+def test_set_producers_checks_its_settings():
+    session = ops.AttentionSession(PRODUCER_KINDS, 1, 8, **SHAPE)
+    with pytest.raises(abi.LlmiError) as err:
+        session.set_producers(rotary_dim=63)          # odd rotary width
+    assert err.value.status == abi.LLMI_UNSUPPORTED
+    with pytest.raises(abi.LlmiError) as err:
+        session.set_producers(conv_kernel=1)          # no conv history
+    assert err.value.status == abi.LLMI_UNSUPPORTED
+    session.set_producers()
+    with pytest.raises(abi.LlmiError) as err:
+        session.set_producers()                       # once per session
+    assert err.value.status == abi.LLMI_INVALID_ARGUMENT
+    assert not session.read_state(0, abi.STATE_CONV_HISTORY).any()
+    session.close()
