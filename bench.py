@@ -93,8 +93,8 @@ def profile_traffic(name: str):
 
 
 class ClockSampler:
-    """SM clocks and clock-event (throttle) reasons sampled every 100 ms during the timed
-    region, read through NVML (read-only queries)."""
+    """SM clocks and clock-event (throttle) reasons sampled every 10 ms during the timed
+    region and once more as it ends, read through NVML (read-only queries)."""
 
     REASONS = {  # NVML clocks-event reason bits
         0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
@@ -135,15 +135,20 @@ class ClockSampler:
                 return getattr(n, name)(self.handle)
         return 0
 
+    def _sample(self):
+        try:
+            sm = self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+            self.samples.append((sm, self._reasons()))
+            return True
+        except Exception as exc:
+            self.error = str(exc)
+            return False
+
     def _run(self):
         while not self.stop.is_set():
-            try:
-                sm = self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
-                self.samples.append((sm, self._reasons()))
-            except Exception as exc:
-                self.error = str(exc)
+            if not self._sample():
                 return
-            self.stop.wait(0.1)
+            self.stop.wait(0.01)
 
     def __enter__(self):
         if self.thread is not None:
@@ -154,6 +159,7 @@ class ClockSampler:
         self.stop.set()
         if self.thread is not None:
             self.thread.join(timeout=2)
+            self._sample()  # the end of the region
 
     def summary(self):
         if not self.samples:
