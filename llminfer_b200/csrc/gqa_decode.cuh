@@ -15,13 +15,16 @@
 //  * The merge pass combines the records of each (sequence, kv head)
 //    (log-sum-exp) and writes the fp16 output.
 //
-// Three partial-pass kernels:
+// Four partial-pass kernels:
 //  * partial_rows: a worker is a CTA and a unit a sequence.  A producer warp
 //    fetches whole cache rows (all kv heads of one key, 2 KiB for Hkv 4 x
 //    D 256) with one bulk copy each into a CTA-wide ring; warp h computes kv
 //    head h.  Used when Hkv * D * 2 == 2048.
-//  * partial_mma: a worker is a warp (or, when Hkv equals the warps of a CTA,
-//    the CTA) with private per-warp pipelines of 512-byte row copies.
+//  * partial_mma: when Hkv equals the warps of a CTA, the CTA is a worker and
+//    warp h serves kv head h, with private per-warp pipelines of 512-byte row
+//    copies.
+//  * partial_mma_cta: otherwise the CTA is a worker whose warps take a unit's
+//    tiles in turn and combine into one record per unit.
 //  * partial_simt: CUDA cores, any head_dim <= 512 and any group.
 //
 // Scores and the softmax stay in fp32 (log2 domain).  Probabilities enter the
@@ -412,6 +415,159 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
   for (uint32_t r = t; r < min(end, t + STAGES); ++r) {
     const uint32_t j = r - begin;
     mbar_wait(&bars[j % STAGES], (j / STAGES) & 1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// partial_mma_cta: the same tile math with the CTA as the worker, for heads ==
+// 1 (a unit is one (sequence, kv head)).  With warps as workers, a unit with
+// few sequences or kv heads per GPU is split over dozens of warps and the
+// merge then walks dozens of records; here the CTA's warps take the unit's
+// tiles in turn (warp w: the CTA's tiles t0 + w, t0 + w + WARPS, ... of the
+// unit), each with its own ring of copies, and at the end of every unit they
+// combine their online-softmax states through shared memory into one record
+// (max over the warps, sums and outputs rescaled by 2^(m_w - m)).  Every
+// warp reaches every unit's barriers: a warp whose bounded wait gave up
+// keeps taking part without computing, and the error word reports it.
+template <int D, int WARPS, int STAGES>
+struct MmaCtaShape {
+  using Base = MmaShape<D, WARPS, STAGES>;
+  static constexpr int kStatesOffset = WARPS * STAGES * Base::kStageBytes + WARPS * STAGES * 8;
+  // + WARPS record-sized state slots (record_floats floats each), sized at launch.
+  static size_t smem_bytes(uint32_t record_floats) {
+    return size_t(kStatesOffset) + size_t(WARPS) * record_floats * sizeof(float);
+  }
+};
+
+template <int D, int WARPS, int STAGES>
+__global__ void __launch_bounds__(WARPS * 32, 1) partial_mma_cta(const Args a) {
+  using Shape = MmaShape<D, WARPS, STAGES>;
+  using CtaShape = MmaCtaShape<D, WARPS, STAGES>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t *stages = smem + warp * STAGES * Shape::kStageBytes;
+  uint64_t *bars =
+      reinterpret_cast<uint64_t *>(smem + WARPS * STAGES * Shape::kStageBytes) + warp * STAGES;
+  float *states = reinterpret_cast<float *>(smem + CtaShape::kStatesOffset);
+
+  const Partition pt = a.pt;  // heads == 1, workers are CTAs
+  pdl_enter();  // before the first global read
+  const uint32_t worker = blockIdx.x;
+  const uint32_t total = pt.units * pt.tiles_per_unit;
+  const uint32_t begin = min(total, worker * pt.tiles_per_worker);
+  const uint32_t end = min(total, begin + pt.tiles_per_worker);
+  if (begin >= end)
+    return;  // uniform over the CTA
+
+  if (lane == 0) {
+    for (int s = 0; s < STAGES; ++s)
+      mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+
+  const uint64_t policy = policy_evict_first();
+  const uint32_t tpu = pt.tiles_per_unit;
+  const uint32_t G = a.group, F = a.record_floats;
+  const uint32_t u_first = begin / tpu, u_last = (end - 1) / tpu;
+
+  // This warp's tiles, unit by unit: (unit u, tile t) with t running over
+  // [max(begin, u*tpu) + warp, min(end, (u+1)*tpu)) in steps of WARPS.
+  struct Cursor {
+    uint32_t u, t;
+  };
+  auto settle = [&](Cursor &c) {  // move past units this warp has no tile left in
+    while (c.u <= u_last && c.t >= min(end, (c.u + 1) * tpu)) {
+      ++c.u;
+      c.t = max(begin, c.u * tpu) + warp;
+    }
+  };
+  auto step = [&](Cursor &c) {
+    c.t += WARPS;
+    settle(c);
+  };
+  auto issue = [&](uint32_t tile, int stage) {
+    const uint32_t unit = tile / tpu, key0 = (tile % tpu) * kTileKeys;
+    const uint32_t seq = unit / a.kv_heads, kvh = unit % a.kv_heads;
+    const uint32_t valid = min(uint32_t(kTileKeys), a.keys - key0);
+    if (lane == 0)
+      mbar_arrive_expect_tx(&bars[stage], 2 * kTileKeys * Shape::kRowBytes);
+    __syncwarp();
+    const uint32_t row = lane & 15;
+    const uint32_t key = key0 + min(row, valid - 1);
+    const __half *src = (lane < 16 ? a.k : a.v) + seq * a.cache_stride +
+                        (size_t(key) * a.kv_heads + kvh) * D;
+    uint8_t *dst = stages + stage * Shape::kStageBytes + (lane < 16 ? 0 : Shape::kTileBytes) +
+                   row * Shape::kRowStride;
+    bulk_g2s(dst, src, Shape::kRowBytes, &bars[stage], policy);
+  };
+
+  // The copy ring runs STAGES tiles ahead of the compute cursor.
+  Cursor ahead{u_first, max(begin, u_first * tpu) + warp};
+  settle(ahead);
+  uint32_t issued = 0, done = 0;  // tiles of this warp issued / computed
+  for (int s = 0; s < STAGES && ahead.u <= u_last; ++s) {
+    issue(ahead.t, s);
+    ++issued;
+    step(ahead);
+  }
+  Cursor cur{u_first, max(begin, u_first * tpu) + warp};
+  settle(cur);
+  bool ok = true;
+  TileMath<D> math;
+  for (uint32_t u = u_first; u <= u_last; ++u) {
+    const uint32_t seq = u / a.kv_heads, kvh = u % a.kv_heads;
+    math.start(a.q + (size_t(seq) * a.kv_heads * G + kvh * G) * D, G, lane);
+    while (ok && cur.u == u) {
+      const int stage = done % STAGES;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars[stage], (done / STAGES) & 1));
+      if (!ok)
+        break;
+      const uint32_t kbase = smem_u32(stages + stage * Shape::kStageBytes);
+      const uint32_t valid = min(uint32_t(kTileKeys), a.keys - (cur.t % tpu) * kTileKeys);
+      math.tile(kbase, kbase + Shape::kTileBytes, Shape::kRowStride, valid, a.scale_log2, lane);
+      __syncwarp();  // every lane is done with this stage before it is refilled
+      ++done;
+      step(cur);
+      if (ahead.u <= u_last) {
+        issue(ahead.t, stage);
+        ++issued;
+        step(ahead);
+      }
+    }
+    // This warp's state for unit u (empty if it had no tile of u), then the
+    // CTA's record: m = max m_w, l = sum l_w 2^(m_w - m), O = sum O_w 2^(m_w - m).
+    math.flush(states + warp * F, G, lane);
+    __syncthreads();
+    float *rec = a.records + record_index(pt, worker, u, 0) * F;
+    for (uint32_t i = threadIdx.x; i < G * (D + 1); i += WARPS * 32) {
+      const uint32_t h = i < G ? i : (i - G) / D;
+      float m = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w)
+        m = fmaxf(m, states[w * F + h]);
+      float acc = 0.f;
+      if (i < G) {
+#pragma unroll
+        for (int w = 0; w < WARPS; ++w)
+          acc = fmaf(states[w * F + G + h], fast_exp2(states[w * F + h] - m), acc);
+        rec[h] = m;
+        rec[G + h] = acc;
+      } else {
+        const uint32_t d = (i - G) % D;
+#pragma unroll
+        for (int w = 0; w < WARPS; ++w)
+          acc = fmaf(states[w * F + 2 * G + h * D + d], fast_exp2(states[w * F + h] - m), acc);
+        rec[2 * G + h * D + d] = acc;
+      }
+    }
+    __syncthreads();  // the state slots are reused by the next unit
+  }
+  if (!ok) {
+    // A wait gave up: let the copies already issued land (bounded) before the
+    // shared memory is released.
+    for (uint32_t r = done; r < issued; ++r)
+      mbar_wait(&bars[r % STAGES], (r / STAGES) & 1);
   }
 }
 

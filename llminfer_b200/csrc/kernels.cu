@@ -130,6 +130,7 @@ int check_gqa(const llmi_gqa_params *p, unsigned batch, const void *q, const voi
 
 struct DecodePlan {
   enum Kind { Rows256x4, Rows128x8, Mma256, Mma128, Mma64, Simt } kind = Simt;
+  bool cta_workers = false;  // Mma kinds with heads == 1: partial_mma_cta
   decode::Partition pt{};
   uint32_t record_floats = 0;
   uint32_t grid = 0, threads = 0;
@@ -140,6 +141,9 @@ struct DecodePlan {
 constexpr int kWarps256 = 4, kStages256 = 3;
 constexpr int kWarps128 = 8, kStages128 = 3;
 constexpr int kWarps64 = 8, kStages64 = 4;
+// partial_mma_cta keeps one record-sized state slot per warp in shared
+// memory beside the copy rings, so its rings are shorter for D 256 and 128.
+constexpr int kCtaStages256 = 2, kCtaStages128 = 2, kCtaStages64 = 4;
 constexpr int kRowStages = 3;
 // DeltaUpdate calls with at least this many tokens use the chunked kernel.
 constexpr uint32_t kChunkedMinTokens = 16;
@@ -197,9 +201,19 @@ int plan_decode(const llmi_gqa_params &p, unsigned batch, bool aligned, const De
     }
     // When the kv heads match the warps of a CTA, the CTA is the worker and
     // its warps stream the same key rows of all kv heads (whole cache rows).
+    // Otherwise the CTA is still the worker (partial_mma_cta): its warps take
+    // a unit's tiles in turn and combine into one record, which keeps the
+    // records per unit few when a GPU holds few sequences or kv heads.
     const bool grouped = p.kvHeads == uint32_t(warps);
     const uint32_t part_units = grouped ? batch : units;
-    const uint32_t per_cta = grouped ? 1u : uint32_t(warps);
+    const uint32_t per_cta = 1u;
+    plan.cta_workers = !grouped;
+    if (!grouped) {
+      const size_t floats = plan.record_floats;
+      smem = int(D == 256   ? decode::MmaCtaShape<256, kWarps256, kCtaStages256>::smem_bytes(floats)
+                 : D == 128 ? decode::MmaCtaShape<128, kWarps128, kCtaStages128>::smem_bytes(floats)
+                            : decode::MmaCtaShape<64, kWarps64, kCtaStages64>::smem_bytes(floats));
+    }
     const uint32_t tpu = (keys + decode::kTileKeys - 1) / decode::kTileKeys;
     const uint64_t tiles = uint64_t(part_units) * tpu;
     if (tiles > UINT32_MAX)
@@ -402,9 +416,16 @@ int launch_decode_rows(const DecodePlan &plan, const decode::Args &args, const D
                           plan.threads, plan.smem, stream, args);
 }
 
-template <int D, int WARPS, int STAGES>
+template <int D, int WARPS, int STAGES, int CTA_STAGES>
 int launch_decode_mma(const DecodePlan &plan, const decode::Args &args, const DeviceInfo &dev,
                       cudaStream_t stream) {
+  if (plan.cta_workers) {
+    auto kernel = decode::partial_mma_cta<D, WARPS, CTA_STAGES>;
+    if (int s = allow_smem(reinterpret_cast<const void *>(kernel), plan.smem, dev))
+      return s;
+    return launch_dependent("gqaScores (decode partial, tensor cores, CTA workers)", kernel,
+                            plan.grid, plan.threads, plan.smem, stream, args);
+  }
   auto kernel = decode::partial_mma<D, WARPS, STAGES>;
   if (int s = allow_smem(reinterpret_cast<const void *>(kernel), plan.smem, dev))
     return s;
@@ -547,13 +568,13 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
     status = launch_decode_rows<128, 8, kRowStages>(plan, a, dev, s);
     break;
   case DecodePlan::Mma256:
-    status = launch_decode_mma<256, kWarps256, kStages256>(plan, a, dev, s);
+    status = launch_decode_mma<256, kWarps256, kStages256, kCtaStages256>(plan, a, dev, s);
     break;
   case DecodePlan::Mma128:
-    status = launch_decode_mma<128, kWarps128, kStages128>(plan, a, dev, s);
+    status = launch_decode_mma<128, kWarps128, kStages128, kCtaStages128>(plan, a, dev, s);
     break;
   case DecodePlan::Mma64:
-    status = launch_decode_mma<64, kWarps64, kStages64>(plan, a, dev, s);
+    status = launch_decode_mma<64, kWarps64, kStages64, kCtaStages64>(plan, a, dev, s);
     break;
   case DecodePlan::Simt:
     status = launch_dependent("gqaScores (decode partial, CUDA cores)", decode::partial_simt,
