@@ -19,7 +19,8 @@
 //  * partial_rows: a worker is a CTA and a unit a sequence.  A producer warp
 //    fetches whole cache rows (all kv heads of one key, 2 KiB for Hkv 4 x
 //    D 256) with one bulk copy each into a CTA-wide ring; warp h computes kv
-//    head h.  Used when Hkv * D * 2 == 2048.
+//    head h.  Used for Hkv 4 x D 256 and Hkv 8 x D 128 (2 KiB rows, one CTA
+//    per SM) and Hkv 2 x D 256 (1 KiB rows, two CTAs per SM).
 //  * partial_mma: when Hkv equals the warps of a CTA, the CTA is a worker and
 //    warp h serves kv head h, with private per-warp pipelines of 512-byte row
 //    copies.

@@ -129,7 +129,7 @@ int check_gqa(const llmi_gqa_params *p, unsigned batch, const void *q, const voi
 // ---- decode planning -------------------------------------------------------
 
 struct DecodePlan {
-  enum Kind { Rows256x4, Rows128x8, Mma256, Mma128, Mma64, Simt } kind = Simt;
+  enum Kind { Rows256x4, Rows256x2, Rows128x8, Mma256, Mma128, Mma64, Simt } kind = Simt;
   bool cta_workers = false;  // Mma kinds with heads == 1: partial_mma_cta
   decode::Partition pt{};
   uint32_t record_floats = 0;
@@ -158,13 +158,23 @@ int plan_decode(const llmi_gqa_params &p, unsigned batch, bool aligned, const De
   const uint32_t units = batch * p.kvHeads;
   plan.record_floats = decode::record_floats(G, D);
   const bool fits = G <= 8 && (D == 256 || D == 128 || D == 64);
-  const bool rows = fits && aligned && ((D == 256 && p.kvHeads == 4) || (D == 128 && p.kvHeads == 8));
+  const bool rows = fits && aligned &&
+                    ((D == 256 && (p.kvHeads == 4 || p.kvHeads == 2)) || (D == 128 && p.kvHeads == 8));
+  // CTAs per SM: one for 2 KiB rows, two for the 1 KiB rows of 2 kv heads
+  // (their CTAs have half the consumer warps and half the shared memory).
+  uint32_t ctas_per_sm = 1;
   if (rows) {
-    // Whole 2 KiB cache rows per bulk copy; the CTA is the worker.
-    if (D == 256) {
+    // Whole cache rows (every kv head of one key) per bulk copy; the CTA is
+    // the worker.
+    if (D == 256 && p.kvHeads == 4) {
       plan.kind = DecodePlan::Rows256x4;
       plan.threads = decode::RowShape<256, 4, kRowStages>::kThreads;
       plan.smem = decode::RowShape<256, 4, kRowStages>::kSmemBytes;
+    } else if (D == 256) {
+      plan.kind = DecodePlan::Rows256x2;
+      plan.threads = decode::RowShape<256, 2, kRowStages>::kThreads;
+      plan.smem = decode::RowShape<256, 2, kRowStages>::kSmemBytes;
+      ctas_per_sm = 2;
     } else {
       plan.kind = DecodePlan::Rows128x8;
       plan.threads = decode::RowShape<128, 8, kRowStages>::kThreads;
@@ -175,7 +185,7 @@ int plan_decode(const llmi_gqa_params &p, unsigned batch, bool aligned, const De
     if (tiles > UINT32_MAX)
       return fail(LLMI_UNSUPPORTED, "decode: %llu key tiles exceed 32 bits",
                   (unsigned long long)tiles);
-    const uint64_t workers_max = uint64_t(dev.sm_count);
+    const uint64_t workers_max = uint64_t(dev.sm_count) * ctas_per_sm;
     const uint32_t tpw = uint32_t((tiles + workers_max - 1) / workers_max);
     plan.grid = uint32_t((tiles + tpw - 1) / tpw);
     plan.pt.units = batch;
@@ -563,6 +573,9 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
   switch (plan.kind) {
   case DecodePlan::Rows256x4:
     status = launch_decode_rows<256, 4, kRowStages>(plan, a, dev, s);
+    break;
+  case DecodePlan::Rows256x2:
+    status = launch_decode_rows<256, 2, kRowStages>(plan, a, dev, s);
     break;
   case DecodePlan::Rows128x8:
     status = launch_decode_rows<128, 8, kRowStages>(plan, a, dev, s);

@@ -41,7 +41,7 @@ def decode_noalloc(q, kc, vc, past):
 
 @pytest.mark.parametrize("batch,past,hq,hkv,d", [
     (8, 4096, 16, 4, 256),   # benchmark per-sequence shape, grouped workers
-    (3, 700, 16, 2, 256),    # warp workers
+    (3, 700, 16, 2, 256),    # whole rows of 2 kv heads
     (2, 50, 4, 2, 12),       # CUDA-core partial pass
 ])
 def test_noalloc_decode_matches_workspace_decode(batch, past, hq, hkv, d):
