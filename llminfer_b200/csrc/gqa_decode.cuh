@@ -576,6 +576,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma_cta(const Args a) {
 // partial_simt: shapes outside the tensor-core kernels (any head_dim up to
 // 512, any group).  One CTA per (unit, key split); warps take query heads.
 
+constexpr int kSimtKeys = 4;  // keys per group in partial_simt
+constexpr uint32_t kSimtMinKeys = 128;  // keys per split at least (bounds the records per unit)
+
 __global__ void __launch_bounds__(128) partial_simt(const Args a) {
   constexpr int kMaxPerLane = 16;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -604,27 +607,57 @@ __global__ void __launch_bounds__(128) partial_simt(const Args a) {
       o[i] = 0.f;
     }
     float m = -INFINITY, l = 0.f;
-    for (uint32_t key = k0; key < k1; ++key) {
-      float dot = 0.f;
+    // Keys in groups of kSimtKeys: the group's K and V rows load together
+    // and its dot products reduce side by side, so a group costs one round of
+    // loads; the online softmax rescales once per group, and p is rounded to
+    // fp16 before the P.V product as in the reference's decode.
+    for (uint32_t key0 = k0; key0 < k1; key0 += kSimtKeys) {
+      __half kv[kSimtKeys][kMaxPerLane], vv[kSimtKeys][kMaxPerLane];
 #pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) {
-        const uint32_t d = lane + 32 * i;
-        if (d < D)
-          dot = fmaf(qv[i], __half2float(kbase[key * row + d]), dot);
+      for (int j = 0; j < kSimtKeys; ++j) {
+        const uint32_t key = min(key0 + j, k1 - 1);
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) {
+          const uint32_t d = lane + 32 * i;
+          kv[j][i] = d < D ? kbase[key * row + d] : __float2half(0.f);
+          vv[j][i] = d < D ? vbase[key * row + d] : __float2half(0.f);
+        }
+      }
+      float x[kSimtKeys];
+#pragma unroll
+      for (int j = 0; j < kSimtKeys; ++j) {
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i)
+          dot = fmaf(qv[i], __half2float(kv[j][i]), dot);
+        x[j] = dot;
       }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1)
-        dot += __shfl_xor_sync(0xffffffffu, dot, off);
-      const float x = dot * a.scale_log2;
-      const float n = fmaxf(m, x);
-      const float r = fast_exp2(m - n), p = fast_exp2(x - n);
-      l = l * r + p;
-      const __half ph = __float2half_rn(p);
+#pragma unroll
+        for (int j = 0; j < kSimtKeys; ++j)
+          x[j] += __shfl_xor_sync(0xffffffffu, x[j], off);
+      float n = m;
+#pragma unroll
+      for (int j = 0; j < kSimtKeys; ++j) {
+        x[j] = key0 + j < k1 ? x[j] * a.scale_log2 : -INFINITY;
+        n = fmaxf(n, x[j]);
+      }
+      const float r = fast_exp2(m - n);
+      float p[kSimtKeys];
+      l *= r;
+#pragma unroll
+      for (int j = 0; j < kSimtKeys; ++j) {
+        p[j] = __half2float(__float2half_rn(fast_exp2(x[j] - n)));
+        l += fast_exp2(x[j] - n);
+      }
 #pragma unroll
       for (int i = 0; i < kMaxPerLane; ++i) {
-        const uint32_t d = lane + 32 * i;
-        if (d < D)
-          o[i] = fmaf(__half2float(ph), __half2float(vbase[key * row + d]), o[i] * r);
+        float acc = o[i] * r;
+#pragma unroll
+        for (int j = 0; j < kSimtKeys; ++j)
+          acc = fmaf(p[j], __half2float(vv[j][i]), acc);
+        o[i] = acc;
       }
       m = n;
     }

@@ -245,8 +245,11 @@ int plan_decode(const llmi_gqa_params &p, unsigned batch, bool aligned, const De
     if (D > 512)
       return fail(LLMI_UNSUPPORTED, "decode: head_dim %u above 512", D);
     plan.kind = DecodePlan::Simt;
+    // Enough (unit, split) CTAs to fill the GPU, but at least kSimtMinKeys
+    // keys per split, so that the merge walks few records per unit.
     const uint32_t want = (4u * dev.sm_count + units - 1) / units;
-    const uint32_t splits = std::max(1u, std::min(keys, want));
+    const uint32_t splits =
+        std::max(1u, std::min((keys + decode::kSimtMinKeys - 1) / decode::kSimtMinKeys, want));
     plan.pt.units = units;
     plan.pt.tiles_per_unit = splits;
     plan.pt.tiles_per_worker = 1;
