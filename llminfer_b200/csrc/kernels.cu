@@ -143,7 +143,11 @@ constexpr int kWarps128 = 8, kStages128 = 3;
 constexpr int kWarps64 = 8, kStages64 = 4;
 // partial_mma_cta keeps one record-sized state slot per warp in shared
 // memory beside the copy rings, so its rings are shorter for D 256 and 128.
-constexpr int kCtaStages256 = 2, kCtaStages128 = 2, kCtaStages64 = 4;
+constexpr int kCtaStages256 = 1, kCtaStages128 = 2, kCtaStages64 = 4;
+// Warps per CTA of partial_mma_cta: for D 256 eight warps with one stage each
+// keep as many bytes in flight as four with two, and twice the warps hide
+// the latency of the tile math.
+constexpr int kCtaWarps256 = 8, kCtaWarps128 = kWarps128, kCtaWarps64 = kWarps64;
 constexpr int kRowStages = 3;
 // DeltaUpdate calls with at least this many tokens use the chunked kernel.
 constexpr uint32_t kChunkedMinTokens = 16;
@@ -220,9 +224,10 @@ int plan_decode(const llmi_gqa_params &p, unsigned batch, bool aligned, const De
     plan.cta_workers = !grouped;
     if (!grouped) {
       const size_t floats = plan.record_floats;
-      smem = int(D == 256   ? decode::MmaCtaShape<256, kWarps256, kCtaStages256>::smem_bytes(floats)
-                 : D == 128 ? decode::MmaCtaShape<128, kWarps128, kCtaStages128>::smem_bytes(floats)
-                            : decode::MmaCtaShape<64, kWarps64, kCtaStages64>::smem_bytes(floats));
+      smem = int(D == 256   ? decode::MmaCtaShape<256, kCtaWarps256, kCtaStages256>::smem_bytes(floats)
+                 : D == 128 ? decode::MmaCtaShape<128, kCtaWarps128, kCtaStages128>::smem_bytes(floats)
+                            : decode::MmaCtaShape<64, kCtaWarps64, kCtaStages64>::smem_bytes(floats));
+      warps = D == 256 ? kCtaWarps256 : D == 128 ? kCtaWarps128 : kCtaWarps64;
     }
     const uint32_t tpu = (keys + decode::kTileKeys - 1) / decode::kTileKeys;
     const uint64_t tiles = uint64_t(part_units) * tpu;
@@ -429,11 +434,11 @@ int launch_decode_rows(const DecodePlan &plan, const decode::Args &args, const D
                           plan.threads, plan.smem, stream, args);
 }
 
-template <int D, int WARPS, int STAGES, int CTA_STAGES>
+template <int D, int WARPS, int STAGES, int CTA_WARPS, int CTA_STAGES>
 int launch_decode_mma(const DecodePlan &plan, const decode::Args &args, const DeviceInfo &dev,
                       cudaStream_t stream) {
   if (plan.cta_workers) {
-    auto kernel = decode::partial_mma_cta<D, WARPS, CTA_STAGES>;
+    auto kernel = decode::partial_mma_cta<D, CTA_WARPS, CTA_STAGES>;
     if (int s = allow_smem(reinterpret_cast<const void *>(kernel), plan.smem, dev))
       return s;
     return launch_dependent("gqaScores (decode partial, tensor cores, CTA workers)", kernel,
@@ -584,13 +589,13 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
     status = launch_decode_rows<128, 8, kRowStages>(plan, a, dev, s);
     break;
   case DecodePlan::Mma256:
-    status = launch_decode_mma<256, kWarps256, kStages256, kCtaStages256>(plan, a, dev, s);
+    status = launch_decode_mma<256, kWarps256, kStages256, kCtaWarps256, kCtaStages256>(plan, a, dev, s);
     break;
   case DecodePlan::Mma128:
-    status = launch_decode_mma<128, kWarps128, kStages128, kCtaStages128>(plan, a, dev, s);
+    status = launch_decode_mma<128, kWarps128, kStages128, kCtaWarps128, kCtaStages128>(plan, a, dev, s);
     break;
   case DecodePlan::Mma64:
-    status = launch_decode_mma<64, kWarps64, kStages64, kCtaStages64>(plan, a, dev, s);
+    status = launch_decode_mma<64, kWarps64, kStages64, kCtaWarps64, kCtaStages64>(plan, a, dev, s);
     break;
   case DecodePlan::Simt:
     status = launch_dependent("gqaScores (decode partial, CUDA cores)", decode::partial_simt,
