@@ -219,11 +219,25 @@ def step_bytes(cfg_kinds, tokens, past, capacity, batch, **shape):
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline (oracle port, every core)
+# CPU baselines: the oracle port (oracle/oracle.c), the reference's scalar
+# check code restated in C.  Nothing here loads llminfer_b200: the bytes and
+# MACs are priced by the oracle's own restatement of the reference cost model.
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def native_oracle():
+    """The oracle built -O3 -march=native on this host (portable build as a fallback),
+    with OpenMP set to every core this process may use (a launcher such as torchrun
+    sets OMP_NUM_THREADS=1 for its workers)."""
     import importlib
+    cores = host_cores()
+    os.environ["OMP_NUM_THREADS"] = str(cores)
     sys.path.insert(0, str(ROOT / "tests"))
     oracle = importlib.import_module("_oracle")
     out = Path(tempfile.gettempdir()) / f"llmi_oracle_native_{os.getpid()}.so"
@@ -235,35 +249,108 @@ def native_oracle():
     except (subprocess.CalledProcessError, OSError):
         lib = oracle.load()
         flags = "-O3"
+    lib.oracle_set_threads(cores)
     oracle._lib = lib
-    return oracle, flags
+    return oracle, flags, cores
 
 
-def cpu_decode_sample(q, kc, vc, past, target_s=12.0, max_seqs=None):
-    """Times the dense fp64 oracle on n sequences of the decode workload, n chosen so the
-    sample takes about target_s.  Returns (GB/s, seconds, n, threads, flags)."""
+def c2_step_bytes(oracle, sequences: int) -> int:
+    """Logical bytes of `sequences` sequences of the C2 step (KvAppend + CausalGqa)."""
+    P, Hq, Hkv, D = C2["past"], C2["query_heads"], C2["kv_heads"], C2["head_dim"]
+    kv = sum(oracle.kv_append_bytes(1, Hkv, D))
+    gqa = sum(oracle.gqa_bytes(1, P, Hq, Hkv, D))
+    return (kv + gqa) * sequences
+
+
+def c2_host_inputs(sequences: int):
+    """One seeded sequence of the C2 step repeated `sequences` times (the work does not
+    depend on the values): q [n,1,Hq,D], new rows [n,1,Hkv,D], caches [n,P+1,Hkv,D]."""
     import numpy as np
-    oracle, flags = native_oracle()
-    threads = oracle.lib().oracle_max_threads()
-    max_seqs = q.shape[0] if max_seqs is None else max_seqs
-    rows = past + 1
+    sys.path.insert(0, str(ROOT / "tests"))
+    import _inputs
+    P = C2["past"]
+    q, k, v = _inputs.gqa_case(1, 1, P, C2["query_heads"], C2["kv_heads"], C2["head_dim"],
+                               seed=SEED)
+    rows = np.ascontiguousarray(k[:, P:P + 1])
+    rep = lambda a: np.ascontiguousarray(np.repeat(a, sequences, axis=0))
+    return rep(q), rep(rows), rep(k), rep(v)
 
-    def host(n):
-        return (q[:n].cpu().numpy(), kc[:n, :rows].cpu().numpy(), vc[:n, :rows].cpu().numpy())
 
-    qs, ks, vs = host(1)
+def cpu_c2_step(oracle, inputs, threads: int) -> float:
+    """One C2 step on the host: cacheAppend of the new key and value rows
+    (Reference.metal:295-301), then the dense fp64 causal GQA check
+    (tests/FlashAttentionTest.mm:53-85) over past + 1 rows.  Returns seconds."""
+    import ctypes
+    q, rows, k, v = inputs
+    n, P, row = q.shape[0], C2["past"], C2["kv_heads"] * C2["head_dim"]
     t0 = time.perf_counter()
-    oracle.gqa_dense(qs, ks, vs, past, threads=threads)
-    one = time.perf_counter() - t0
-    n = int(max(1, min(max_seqs, round(target_s / max(one, 1e-6)))))
-    qs, ks, vs = host(n)
-    t0 = time.perf_counter()
-    oracle.gqa_dense(qs, ks, vs, past, threads=threads)
-    secs = time.perf_counter() - t0
-    per_seq = step_bytes([1], 1, past, C2["capacity"], 1, query_heads=C2["query_heads"],
-                         kv_heads=C2["kv_heads"], head_dim=C2["head_dim"])["CausalGqa"][0]
+    for cache in (k, v):
+        oracle.lib().oracle_cache_append(
+            ctypes.c_uint(row), ctypes.c_uint(P * row), ctypes.c_uint(n),
+            rows.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(row),
+            cache.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(cache[0].size))
+    oracle.gqa_dense(q, k, v, P, threads=threads)
+    return time.perf_counter() - t0
+
+
+def cpu_op_baselines(budget_s: float = 4.0):
+    """Every op of the path on the host cores, all cores and one thread, each on a
+    bounded sample of its benchmark config (the CPU baseline table: C1 prefill, C2
+    decode step, C3 DeltaNet prefill, C4 DeltaNet step).  Returns {config: entry}."""
+    import numpy as np
+    sys.path.insert(0, str(ROOT / "tests"))
+    import _inputs
+    oracle, flags, cores = native_oracle()
+    build = f"oracle/oracle.c, gcc {flags} -fopenmp"
+    res = {}
+
+    def timed(fn, threads):
+        t0 = time.perf_counter()
+        fn(threads)
+        return time.perf_counter() - t0
+
+    # C1: dense fp64 GQA, B=1, T=128, past 0 (the whole config).
+    q, k, v = _inputs.gqa_case(1, 128, 0, 16, 4, 256, seed=SEED)
+    flop = 2 * oracle.lib().oracle_gqa_fp_macs(128, 0, 16, 256)
+    run = lambda th: oracle.gqa_dense(q, k, v, 0, threads=th)
+    run(cores)
+    t_all, t_one = timed(run, cores), timed(run, 1)
+    res["C1"] = {"unit": "TFLOP/s", "all_cores": round(flop / t_all / 1e12, 6),
+                 "one_thread": round(flop / t_one / 1e12, 6), "cores": cores,
+                 "sample": f"the whole config; dense fp64 check of FlashAttentionTest.mm:53-85 "
+                           f"({build})"}
+    # C2: the decode step; all cores on the full batch of 64, one thread on 2 sequences.
+    full = c2_host_inputs(C2["batch"])
+    cpu_c2_step(oracle, c2_host_inputs(1), cores)
+    t_all = cpu_c2_step(oracle, full, cores)
+    t_one = cpu_c2_step(oracle, c2_host_inputs(2), 1)
+    res["C2"] = {"unit": "GB/s", "all_cores": round(c2_step_bytes(oracle, 64) / t_all / 1e9, 4),
+                 "one_thread": round(c2_step_bytes(oracle, 2) / t_one / 1e9, 4), "cores": cores,
+                 "sample": f"all cores: the whole step (64 sequences); one thread: 2 sequences; "
+                           f"cacheAppend + dense fp64 GQA ({build})"}
+    del full
+    # C3 and C4: the token-sequential DeltaNet (Graph.metal:146-170 +
+    # Reference.metal:182-197).  Bytes of a sample: the cost model's per-sequence
+    # bytes of a call of that length.
+    def delta_entry(name, tokens_all, seqs_all, tokens_one, seqs_one, std, note):
+        out = {"unit": "GB/s", "cores": cores}
+        for key, T, B, th in (("all_cores", tokens_all, seqs_all, cores),
+                              ("one_thread", tokens_one, seqs_one, 1)):
+            c = _inputs.delta_case(B, T, 16, 128, 32, 128, state_std=std, seed=SEED)
+            nbytes = sum(oracle.delta_bytes(T, 16, 128, 32, 128)) * B
+            secs = timed(lambda th_: oracle.delta_update(c["q"], c["k"], c["v"], c["beta"],
+                                                         c["decay"], c["state"], threads=th_), th)
+            out[key] = round(nbytes / secs / 1e9, 4)
+        out["sample"] = f"{note}; token-sequential DeltaNet ({build})"
+        return out
+
+    res["C3"] = delta_entry("C3", 4096, 1, 256, 1, 0.0,
+                            "all cores: 1 of the 4 sequences, all 4096 tokens; one thread: 1 "
+                            "sequence, 256 tokens")
+    res["C4"] = delta_entry("C4", 1, 256, 1, 16, 0.02,
+                            "all cores: the whole step (256 sequences); one thread: 16 sequences")
     del np
-    return per_seq * n / secs / 1e9, secs, n, threads, flags
+    return res
 
 
 # ---------------------------------------------------------------------------
@@ -410,18 +497,22 @@ def run_ours(args, dist):
     d2h = out.numel() * 2
 
     cpu = None
+    cpu_ops = {}
     if not args.no_cpu and dist.world == 1 and dist.rank == 0:
-        gbs, secs, n, threads, flags = cpu_decode_sample(q, kc, vc, P)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{n} of 64 sequences of the C2 decode step (CausalGqa), "
-                         f"{secs:.1f} s; dense fp64 check of tests/FlashAttentionTest.mm:53-85 "
-                         f"restated in oracle/oracle.c, gcc {flags} -fopenmp"}
+        cpu_ops = cpu_op_baselines()
+        c2 = cpu_ops["C2"]
+        cpu = {"value": c2["all_cores"], "unit": "GB/s", "cores": c2["cores"], "kind": "port",
+               "one_thread_value": c2["one_thread"], "sample": c2["sample"]}
 
     del q, kn, vn, kc, vc, out, ws, hq, hk, hv, hout, dq, dk, dv, dout
     torch.cuda.empty_cache()
     secondary = []
     if not args.no_secondary:
         secondary = run_secondary(torch, ops, device, peaks, dist)
+        for entry in secondary:
+            tag = entry["workload"].split(" ")[0]
+            if tag in cpu_ops:
+                entry["cpu_baseline"] = cpu_ops[tag]
     stack = None
     if not args.no_stack:
         from llminfer_b200.stack import run_stack
@@ -650,52 +741,42 @@ def run_secondary(torch, ops, device, peaks, dist):
 # reference arm
 
 
-def run_reference(args, dist):
-    import numpy as np
-    if dist.rank != 0:
+def run_reference(args):
+    """The reference arm: the reference's scalar check code for the C2 step, restated in
+    oracle/ (the reference's own path is Metal and cannot run here), on every host core.
+    Each timed step is the whole C2 step (64 sequences), the same work at every N; under
+    torchrun only rank 0 runs it, the other ranks exit without work."""
+    if int(os.environ.get("RANK", "0")) != 0:
         return None
-    sys.path.insert(0, str(ROOT / "tests"))
-    import _inputs
-    oracle, flags = native_oracle()
-    threads = oracle.lib().oracle_max_threads()
-    P = C2["past"]
-    # One step = a bounded sample of the C2 decode workload: n sequences.
-    q, k, v = _inputs.gqa_case(1, 1, P, C2["query_heads"], C2["kv_heads"], C2["head_dim"],
-                               seed=SEED)
-    t0 = time.perf_counter()
-    oracle.gqa_dense(q, k, v, P, threads=threads)
-    one = time.perf_counter() - t0
-    n = int(max(1, min(C2["batch"], round(1.5 / max(one, 1e-6)))))
-    qs = np.repeat(q, n, axis=0)
-    ks = np.repeat(k, n, axis=0)
-    vs = np.repeat(v, n, axis=0)
-    per_seq = step_bytes([1], 1, P, C2["capacity"], 1, query_heads=C2["query_heads"],
-                         kv_heads=C2["kv_heads"], head_dim=C2["head_dim"])
-    bytes_seq = per_seq["KvAppend"][0] + per_seq["CausalGqa"][0]
-    for _ in range(args.warmup):
-        oracle.gqa_dense(qs[:1], ks[:1], vs[:1], P, threads=threads)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        oracle.gqa_dense(qs, ks, vs, P, threads=threads)
-        times.append(time.perf_counter() - t0)
+    oracle, flags, cores = native_oracle()
+    full = c2_host_inputs(C2["batch"])
+    for _ in range(max(args.warmup, 1)):
+        cpu_c2_step(oracle, full, cores)
+    times = [cpu_c2_step(oracle, full, cores) for _ in range(args.steps)]
     secs = sum(times)
-    value = bytes_seq * n * args.steps / secs / 1e9
-    sample = (f"{n} of the 64 sequences of the C2 decode step per timed step, dense fp64 causal "
-              f"GQA (tests/FlashAttentionTest.mm:53-85 restated in oracle/oracle.c, gcc {flags} "
-              f"-fopenmp); the reference's own path is Metal and cannot run here")
+    value = c2_step_bytes(oracle, C2["batch"]) * args.steps / secs / 1e9
+    one_secs = cpu_c2_step(oracle, c2_host_inputs(2), 1)
+    one_value = c2_step_bytes(oracle, 2) / one_secs / 1e9
+    sample = (f"each step the whole C2 step: cacheAppend of the new rows and the dense fp64 "
+              f"causal GQA of all 64 sequences (tests/FlashAttentionTest.mm:53-85, "
+              f"Reference.metal:295-301 restated in oracle/oracle.c, gcc {flags} -fopenmp, "
+              f"{cores} threads); the reference's own path is Metal and cannot run here")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     return {
         "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "impl": "reference",
-        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(secs / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic: seeded N(0,1) fp16 (numpy Philox)",
-        "config": {"workload": "C2 GQA decode step, bounded sample (see cpu_baseline.sample)",
-                   "global_batch": C2["batch"], "past": P, "capacity": C2["capacity"],
+        "config": {"workload": "C2 GQA decode step (cacheAppend x2 + causal GQA): batch 64, "
+                               "1 new token, past 4096, Hq 16, Hkv 4, D 256",
+                   "global_batch": C2["batch"], "past": C2["past"], "capacity": C2["capacity"],
                    "query_heads": C2["query_heads"], "kv_heads": C2["kv_heads"],
-                   "head_dim": C2["head_dim"], "parallelism": "host cores (OpenMP)"},
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
+                   "head_dim": C2["head_dim"], "parallelism": f"host cores (OpenMP, {cores})"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores,
                          "kind": "port", "sample": sample},
+        "cpu_one_thread": {"value": round(one_value, 4), "unit": "GB/s", "cores": 1,
+                           "sample": "2 sequences of the C2 step on one thread"},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
@@ -709,12 +790,16 @@ def main():
     result_out = os.fdopen(os.dup(sys.stdout.fileno()), "w")
     sys.stdout.flush()
     os.dup2(sys.stderr.fileno(), sys.stdout.fileno())
+    if args.impl == "reference":
+        # No process group and no GPU work: rank 0 times the host cores, the
+        # other ranks exit at once.
+        line = run_reference(args)
+        if line is not None:
+            print(json.dumps(line), file=result_out, flush=True)
+        return
     dist = Dist(args.gpus)
     try:
-        if args.impl == "reference":
-            line = run_reference(args, dist)
-        else:
-            line = run_ours(args, dist)
+        line = run_ours(args, dist)
         if dist.rank == 0 and line is not None:
             print(json.dumps(line), file=result_out, flush=True)
     finally:

@@ -630,8 +630,11 @@ namespace {
 // with cudaGetSymbolAddress while that device is current, and cached.
 int static_decode_scratch(const DeviceInfo &dev, void **address) {
   static std::mutex mutex;
-  static void *cached[64] = {};
+  static void *cached[kMaxDevices] = {};
   std::lock_guard<std::mutex> lock(mutex);
+  if (dev.device < 0 || dev.device >= kMaxDevices)
+    return fail(LLMI_INVALID_ARGUMENT, "decode_noalloc: device %d outside [0, %d)", dev.device,
+                kMaxDevices);
   if (!cached[dev.device]) {
     void *p = nullptr;
     if (int s = check_cuda(cudaGetSymbolAddress(&p, g_static_decode_scratch),

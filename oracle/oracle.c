@@ -105,6 +105,36 @@ static int pick_threads(int threads) {
 
 /* ---- GQA ------------------------------------------------------------------ */
 
+/* One query row of the dense fp64 check (FlashAttentionTest.mm:53-85): the
+ * row's scores against keys [0, visible), exact softmax, weighted values.
+ * k and v point at the row's kv head in a cache of kv_row-element rows;
+ * weights holds `visible` doubles. */
+static void dense_row(const uint16_t *qr, const uint16_t *ks, const uint16_t *vs,
+                      size_t kv_row, unsigned D, unsigned visible, double *weights,
+                      double *o) {
+  const double inv_sqrt = 1.0 / sqrt((double)D);
+  double top = -INFINITY;
+  for (unsigned i = 0; i < visible; ++i) {
+    double dot = 0.0;
+    for (unsigned d = 0; d < D; ++d)
+      dot += (double)oracle_f16_to_f32(qr[d]) * oracle_f16_to_f32(ks[i * kv_row + d]);
+    weights[i] = dot * inv_sqrt;
+    if (weights[i] > top)
+      top = weights[i];
+  }
+  double total = 0.0;
+  for (unsigned i = 0; i < visible; ++i) {
+    weights[i] = exp(weights[i] - top);
+    total += weights[i];
+  }
+  for (unsigned d = 0; d < D; ++d) {
+    double acc = 0.0;
+    for (unsigned i = 0; i < visible; ++i)
+      acc += weights[i] * oracle_f16_to_f32(vs[i * kv_row + d]);
+    o[d] = acc / total;
+  }
+}
+
 void oracle_gqa_dense(const oracle_gqa_params *p, unsigned batch,
                       const uint16_t *q, size_t q_stride, const uint16_t *k,
                       const uint16_t *v, size_t kv_stride, double *out,
@@ -113,7 +143,6 @@ void oracle_gqa_dense(const oracle_gqa_params *p, unsigned batch,
   const unsigned group = p->queryHeads / p->kvHeads;
   const size_t kv_row = (size_t)p->kvHeads * D;
   const long rows = (long)batch * p->tokens * Hq;
-  const double inv_sqrt = 1.0 / sqrt((double)D);
 #pragma omp parallel num_threads(pick_threads(threads))
   {
     double *weights = (double *)malloc(sizeof(double) * (p->past + p->tokens + 1));
@@ -122,32 +151,31 @@ void oracle_gqa_dense(const oracle_gqa_params *p, unsigned batch,
       unsigned seq = (unsigned)(r / ((long)p->tokens * Hq));
       unsigned row = (unsigned)(r % ((long)p->tokens * Hq)); /* token*Hq + head */
       unsigned token = row / Hq, head = row % Hq;
-      unsigned visible = p->past + token + 1;
-      const uint16_t *qr = q + seq * q_stride + (size_t)row * D;
-      const uint16_t *ks = k + seq * kv_stride + (size_t)(head / group) * D;
-      const uint16_t *vs = v + seq * kv_stride + (size_t)(head / group) * D;
-      double top = -INFINITY;
-      for (unsigned i = 0; i < visible; ++i) {
-        double dot = 0.0;
-        for (unsigned d = 0; d < D; ++d)
-          dot += (double)oracle_f16_to_f32(qr[d]) * oracle_f16_to_f32(ks[i * kv_row + d]);
-        weights[i] = dot * inv_sqrt;
-        if (weights[i] > top)
-          top = weights[i];
-      }
-      double total = 0.0;
-      for (unsigned i = 0; i < visible; ++i) {
-        weights[i] = exp(weights[i] - top);
-        total += weights[i];
-      }
-      double *o = out + ((size_t)seq * p->tokens * Hq + row) * D;
-      for (unsigned d = 0; d < D; ++d) {
-        double acc = 0.0;
-        for (unsigned i = 0; i < visible; ++i)
-          acc += weights[i] * oracle_f16_to_f32(vs[i * kv_row + d]);
-        o[d] = acc / total;
-      }
+      dense_row(q + seq * q_stride + (size_t)row * D,
+                k + seq * kv_stride + (size_t)(head / group) * D,
+                v + seq * kv_stride + (size_t)(head / group) * D, kv_row, D,
+                p->past + token + 1, weights,
+                out + ((size_t)seq * p->tokens * Hq + row) * D);
     }
+    free(weights);
+  }
+}
+
+void oracle_gqa_dense_rows(const oracle_gqa_params *p, const uint16_t *q_rows,
+                           const uint16_t *k, const uint16_t *v,
+                           const unsigned *token, const unsigned *head, unsigned n,
+                           double *out, int threads) {
+  const unsigned D = p->headDim;
+  const unsigned group = p->queryHeads / p->kvHeads;
+  const size_t kv_row = (size_t)p->kvHeads * D;
+#pragma omp parallel num_threads(pick_threads(threads))
+  {
+    double *weights = (double *)malloc(sizeof(double) * (p->past + p->tokens + 1));
+#pragma omp for schedule(dynamic, 1)
+    for (long r = 0; r < (long)n; ++r)
+      dense_row(q_rows + (size_t)r * D, k + (size_t)(head[r] / group) * D,
+                v + (size_t)(head[r] / group) * D, kv_row, D, p->past + token[r] + 1,
+                weights, out + (size_t)r * D);
     free(weights);
   }
 }
@@ -362,4 +390,40 @@ uint64_t oracle_gqa_fp_macs(uint64_t tokens, uint64_t past, uint64_t queryHeads,
 uint64_t oracle_delta_fp_macs(uint64_t tokens, uint64_t valueHeads,
                               uint64_t keyDim, uint64_t valueDim) {
   return 3 * tokens * valueHeads * keyDim * valueDim;
+}
+
+/* Logical bytes: operands read and written once (Cost.cpp:85-93). */
+void oracle_kv_append_bytes(uint64_t tokens, uint64_t kvHeads, uint64_t headDim,
+                            uint64_t *read, uint64_t *write) {
+  /* new keys and values [T][Hkv][D] f16 in; the same rows written. */
+  *read = 2 * tokens * kvHeads * headDim * 2;
+  *write = *read;
+}
+
+void oracle_gqa_bytes(uint64_t tokens, uint64_t past, uint64_t queryHeads, uint64_t kvHeads,
+                      uint64_t headDim, uint64_t *read, uint64_t *write) {
+  /* q [T][Hq][D] f16 and cache rows [0, past+T) of K and V in; out like q. */
+  const uint64_t q_bytes = tokens * queryHeads * headDim * 2;
+  *read = q_bytes + 2 * (past + tokens) * kvHeads * headDim * 2;
+  *write = q_bytes;
+}
+
+void oracle_delta_bytes(uint64_t tokens, uint64_t keyHeads, uint64_t keyDim,
+                        uint64_t valueHeads, uint64_t valueDim, uint64_t *read,
+                        uint64_t *write) {
+  /* q, k f32; v f16; beta, decay f32; the state read once and written once;
+   * out f16. */
+  const uint64_t state = valueHeads * keyDim * valueDim * 4;
+  *read = 2 * tokens * keyHeads * keyDim * 4 + tokens * valueHeads * valueDim * 2 +
+          2 * tokens * valueHeads * 4 + state;
+  *write = tokens * valueHeads * valueDim * 2 + state;
+}
+
+void oracle_set_threads(int threads) {
+#ifdef _OPENMP
+  if (threads > 0)
+    omp_set_num_threads(threads);
+#else
+  (void)threads;
+#endif
 }

@@ -58,6 +58,15 @@ void oracle_gqa_dense(const oracle_gqa_params *p, unsigned batch,
                       const uint16_t *v, size_t kv_stride, double *out,
                       int threads);
 
+/* The same check for n chosen rows of ONE sequence, for shapes whose full
+ * output is too large to compute on a CPU: row r is query token token[r],
+ * query head head[r], with its q row at q_rows[r*headDim] and the sequence's
+ * cache rows in k, v ([rows][kvHeads][headDim] fp16).  out: [n][headDim]. */
+void oracle_gqa_dense_rows(const oracle_gqa_params *p, const uint16_t *q_rows,
+                           const uint16_t *k, const uint16_t *v,
+                           const unsigned *token, const unsigned *head, unsigned n,
+                           double *out, int threads);
+
 /* The reference's non-flash path with its fp16 rounding points:
  * gqaScores (Reference.metal:303-323): s = half(half(q.k) * rsqrt(D));
  * gqaSoftmax (Graph.metal:172-210): p = half(exp(s - max) / sum);
@@ -141,6 +150,18 @@ uint64_t oracle_gqa_fp_macs(uint64_t tokens, uint64_t past, uint64_t queryHeads,
                             uint64_t headDim);
 uint64_t oracle_delta_fp_macs(uint64_t tokens, uint64_t valueHeads,
                               uint64_t keyDim, uint64_t valueDim);
+/* Logical bytes read and written by one sequence's op (same model). */
+void oracle_kv_append_bytes(uint64_t tokens, uint64_t kvHeads, uint64_t headDim,
+                            uint64_t *read, uint64_t *write);
+void oracle_gqa_bytes(uint64_t tokens, uint64_t past, uint64_t queryHeads, uint64_t kvHeads,
+                      uint64_t headDim, uint64_t *read, uint64_t *write);
+void oracle_delta_bytes(uint64_t tokens, uint64_t keyHeads, uint64_t keyDim,
+                        uint64_t valueHeads, uint64_t valueDim, uint64_t *read,
+                        uint64_t *write);
+
+/* Sets the OpenMP thread count used when a call passes threads <= 0 (a
+ * launcher may have set OMP_NUM_THREADS=1 for the process). */
+void oracle_set_threads(int threads);
 
 /* Number of threads oracle_* would use for `threads` <= 0. */
 int oracle_max_threads(void);

@@ -60,6 +60,10 @@ def load(path: Path | None = None) -> ctypes.CDLL:
     lib.oracle_gqa_fp_macs.argtypes = [c_uint64] * 4
     lib.oracle_delta_fp_macs.restype = c_uint64
     lib.oracle_delta_fp_macs.argtypes = [c_uint64] * 4
+    lib.oracle_kv_append_bytes.argtypes = [c_uint64] * 3 + [POINTER(c_uint64)] * 2
+    lib.oracle_gqa_bytes.argtypes = [c_uint64] * 5 + [POINTER(c_uint64)] * 2
+    lib.oracle_delta_bytes.argtypes = [c_uint64] * 5 + [POINTER(c_uint64)] * 2
+    lib.oracle_set_threads.argtypes = [c_int]
     return lib
 
 
@@ -111,6 +115,23 @@ def gqa_dense(q, k_cache, v_cache, past: int, threads: int = 0) -> np.ndarray:
     lib().oracle_gqa_dense(ctypes.byref(p), c_uint(B), _ptr(q, c_uint16), c_size_t(T * Hq * D),
                            _ptr(k, c_uint16), _ptr(v, c_uint16), c_size_t(k[0].size),
                            _ptr(out, c_double), c_int(threads))
+    return out
+
+
+def gqa_dense_rows(q_rows, k_seq, v_seq, past: int, tokens: int, query_heads: int,
+                   token, head, threads: int = 0) -> np.ndarray:
+    """fp64 dense causal GQA of chosen rows of one sequence.  q_rows [n,D] are
+    the rows (token[i], head[i]); k_seq/v_seq [rows,Hkv,D] that sequence's
+    cache.  Returns [n,D] float64."""
+    q, k, v = _as_bits(q_rows), _as_bits(k_seq), _as_bits(v_seq)
+    n, D = q.shape
+    token = np.ascontiguousarray(token, np.uint32)
+    head = np.ascontiguousarray(head, np.uint32)
+    p = GqaParams(tokens, query_heads, k.shape[1], D, past)
+    out = np.empty((n, D), dtype=np.float64)
+    lib().oracle_gqa_dense_rows(ctypes.byref(p), _ptr(q, c_uint16), _ptr(k, c_uint16),
+                                _ptr(v, c_uint16), _ptr(token, c_uint), _ptr(head, c_uint),
+                                c_uint(n), _ptr(out, c_double), c_int(threads))
     return out
 
 
@@ -232,3 +253,24 @@ def reference_shim():
     ref.ref_attention_costs.restype = c_int
     ref.ref_attention_costs.argtypes = [c_uint64] * 10 + [POINTER(c_uint64)]
     return ref
+
+
+def _bytes(fn, *args) -> tuple[int, int]:
+    r, w = c_uint64(), c_uint64()
+    fn(*args, ctypes.byref(r), ctypes.byref(w))
+    return r.value, w.value
+
+
+def kv_append_bytes(tokens, kv_heads, head_dim) -> tuple[int, int]:
+    """(read, write) logical bytes of one sequence's KvAppend (Cost.cpp:85-93)."""
+    return _bytes(lib().oracle_kv_append_bytes, tokens, kv_heads, head_dim)
+
+
+def gqa_bytes(tokens, past, query_heads, kv_heads, head_dim) -> tuple[int, int]:
+    """(read, write) logical bytes of one sequence's CausalGqa."""
+    return _bytes(lib().oracle_gqa_bytes, tokens, past, query_heads, kv_heads, head_dim)
+
+
+def delta_bytes(tokens, key_heads, key_dim, value_heads, value_dim) -> tuple[int, int]:
+    """(read, write) logical bytes of one sequence's DeltaUpdate."""
+    return _bytes(lib().oracle_delta_bytes, tokens, key_heads, key_dim, value_heads, value_dim)

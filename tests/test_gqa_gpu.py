@@ -89,7 +89,9 @@ def test_prefill_matches_dense_oracle(batch, tokens, past, hq, hkv, d):
     (2, 16, 16, 4, 256),
     (2, 1000, 16, 4, 256),
     (2, 77, 8, 8, 128),
-    (2, 300, 16, 2, 256),      # group of 8 query heads
+    (2, 300, 16, 2, 256),      # group of 8, 2 kv heads: the whole-row pass of 1 KiB rows
+    (2, 300, 8, 1, 256),       # group of 8 on the 8-warp CTA-worker pass (heads 4-7 in the combine)
+    (2, 1000, 24, 3, 256),     # group of 8, 3 kv heads: CTA workers over units of 3 heads
     (2, 33, 8, 1, 64),
     (2, 40, 16, 8, 64),        # CTA workers with per-warp pipelines
     (2, 50, 4, 2, 12),         # odd head_dim (CUDA-core path)

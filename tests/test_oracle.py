@@ -106,6 +106,18 @@ def test_dense_gqa_batch_and_threads_are_consistent():
         np.testing.assert_array_equal(single, one[b:b + 1])
 
 
+def test_dense_gqa_rows_equal_the_full_check():
+    # The sampled-rows form (used where the full output is too large for a
+    # CPU) gives the full check's rows bit for bit.
+    q, k, v = _inputs.gqa_case(2, 40, 10, 8, 2, 64, seed=3)
+    full = _oracle.gqa_dense(q, k, v, 10)
+    token = np.array([0, 5, 39, 20, 39])
+    head = np.array([7, 0, 3, 5, 0])
+    for b in range(2):
+        rows = _oracle.gqa_dense_rows(q[b, token, head], k[b], v[b], 10, 40, 8, token, head)
+        np.testing.assert_array_equal(rows, full[b, token, head])
+
+
 def test_delta_oracle_matches_transformers_recurrent_rule():
     d = np.load(GOLDEN / "delta_xcheck.npz")
     out, state = _oracle.delta_update(d["q"], d["k"], d["v"].view(np.float16), d["beta"],
@@ -140,3 +152,25 @@ def test_cost_model_pins():
     # tests/ConverterTest.py:186: T=3, two value heads of 4 x 4.
     assert lib.oracle_delta_fp_macs(3, 2, 4, 4) == 288
     assert lib.oracle_gqa_pairs(128, 0) == 8256
+
+
+def test_cost_model_matches_reference_records(pins):
+    # The oracle's cost formulas (used to price the CPU baseline) against the
+    # records of the reference's own GraphIR cost model compiled from source.
+    fields = pins["attention_costs"]["fields"]
+    checked = 0
+    for case in pins["attention_costs"]["cases"]:
+        if case["status"] != 0:
+            continue
+        tokens, past, _ = case["step"]
+        hq, hkv, d, hk, dk, hv, dv = case["shape"]
+        want = dict(zip(fields, case["record"]))
+        assert _oracle.kv_append_bytes(tokens, hkv, d)[1] == want["kv_write_bytes"]
+        assert _oracle.gqa_bytes(tokens, past, hq, hkv, d) == (want["gqa_read_bytes"],
+                                                                want["gqa_write_bytes"])
+        assert _oracle.lib().oracle_gqa_fp_macs(tokens, past, hq, d) == want["gqa_fp_macs"]
+        assert _oracle.delta_bytes(tokens, hk, dk, hv, dv) == (want["delta_read_bytes"],
+                                                                want["delta_write_bytes"])
+        assert _oracle.lib().oracle_delta_fp_macs(tokens, hv, dk, dv) == want["delta_fp_macs"]
+        checked += 1
+    assert checked >= 20

@@ -43,6 +43,8 @@ def decode_noalloc(q, kc, vc, past):
     (8, 4096, 16, 4, 256),   # benchmark per-sequence shape, grouped workers
     (3, 700, 16, 2, 256),    # whole rows of 2 kv heads
     (2, 50, 4, 2, 12),       # CUDA-core partial pass
+    (8, 2000, 4, 1, 256),    # CTA workers: one record per (worker, unit)
+    (3, 500, 8, 2, 128),     # CTA workers, head_dim 128
 ])
 def test_noalloc_decode_matches_workspace_decode(batch, past, hq, hkv, d):
     q, k, v = _inputs.gqa_case(batch, 1, past, hq, hkv, d, capacity=past + 3, seed=past + d)
