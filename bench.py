@@ -607,6 +607,125 @@ def time_graph(torch, fn, dist, reps=50):
     return ms
 
 
+def delta_inputs(torch, device, g, B, T, Hk, Hv, state_std, dk=128, dv=128):
+    """Seeded DeltaNet operands drawn as the configs say (on the device)."""
+    nrm = torch.nn.functional.normalize
+    q = (nrm(torch.randn(B, T, Hk, dk, generator=g, device=device), dim=-1) / dk ** 0.5)
+    q = q.reshape(B, T, Hk * dk).contiguous()
+    k = nrm(torch.randn(B, T, Hk, dk, generator=g, device=device), dim=-1)
+    k = k.reshape(B, T, Hk * dk).contiguous()
+    v = torch.randn(B, T, Hv * dv, generator=g, device=device).half()
+    beta = torch.sigmoid(torch.randn(B, T, Hv, generator=g, device=device)).half().float()
+    decay = torch.exp(-torch.nn.functional.softplus(
+        torch.randn(B, T, Hv, generator=g, device=device)))
+    state = torch.randn(B, Hv, dk, dv, generator=g, device=device) * state_std
+    return q, k, v, beta, decay, state
+
+
+def run_strong(torch, ops, device, peaks, dist, g):
+    """C2, C3 and C4 split over the ranks (fixed total work).  Returns one line per
+    config: aggregate value (whole job / max-over-ranks time) and, from rank 0's
+    run of the whole job on one GPU, the efficiency against 1 GPU."""
+    N = dist.world
+    out = []
+
+    def measure(make, reps, warmup, whole):
+        fn, nbytes = make(whole)
+        med, _ = time_op(torch, fn, dist, reps=reps, warmup=warmup)
+        return med, nbytes
+
+    def line(name, unit_desc, make, total_bytes, reps=10, warmup=3):
+        ms, _ = measure(make, reps, warmup, whole=False)
+        gbs = total_bytes / (ms / 1e3) / 1e9
+        entry = {"workload": name, "scaling": "strong", "split": unit_desc,
+                 "ms": round(ms, 4), "value": round(gbs, 1), "unit": "GB/s",
+                 "frac_of_hbm_peak_per_gpu": round(gbs / N / peaks["hbm_gbs"], 4)}
+        # The whole job on one GPU (rank 0; the other ranks wait at the barrier).
+        if N > 1:
+            dist.barrier()
+            if dist.rank == 0:
+                fn, _ = make(True)
+                for _ in range(warmup):
+                    fn()
+                torch.cuda.synchronize()
+                evs = [(torch.cuda.Event(enable_timing=True),
+                        torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+                for a, b in evs:
+                    a.record()
+                    fn()
+                    b.record()
+                torch.cuda.synchronize()
+                one = statistics.median(a.elapsed_time(b) for a, b in evs)
+                entry["ms_1gpu"] = round(one, 4)
+                entry["efficiency_vs_1gpu"] = round(one / (N * ms), 4)
+            dist.barrier()
+        else:
+            entry["ms_1gpu"] = round(ms, 4)
+            entry["efficiency_vs_1gpu"] = 1.0
+        torch.cuda.empty_cache()
+        return entry
+
+    # C2: the decode step (two appends + decode) of 64 sequences.
+    P, CAP = C2["past"], C2["capacity"]
+    Hq, Hkv, D = C2["query_heads"], C2["kv_heads"], C2["head_dim"]
+    per_seq = step_bytes([1], 1, P, CAP, 1, query_heads=Hq, kv_heads=Hkv, head_dim=D)
+    seq_bytes = per_seq["KvAppend"][0] + per_seq["CausalGqa"][0]
+
+    def make_c2(whole):
+        B = 64 if whole else 64 // N
+        kc = torch.zeros(B, CAP, Hkv, D, dtype=torch.float16, device=device)
+        vc = torch.zeros_like(kc)
+        kc[:, :P].normal_(generator=g)
+        vc[:, :P].normal_(generator=g)
+        q = torch.randn(B, 1, Hq, D, generator=g, device=device).half()
+        kn = torch.randn(B, 1, Hkv, D, generator=g, device=device).half()
+        o = torch.empty_like(q)
+        ws = torch.empty(ops.decode_workspace_bytes(B, Hq, Hkv, D, P), dtype=torch.uint8,
+                         device=device)
+
+        def fn():
+            ops.cache_append(kn, kc, P)
+            ops.cache_append(kn, vc, P)
+            ops.gqa_decode(q, kc, vc, P, out=o, workspace=ws)
+        return fn, seq_bytes * B
+
+    out.append(line("C2 GQA decode step, 64 sequences in all (cacheAppend x2 + gqaScores + "
+                    "gqaSoftmax)", f"{64 // N} sequences per GPU", make_c2, seq_bytes * 64))
+
+    # C3: DeltaNet prefill, B=4, T=4096, 128 (sequence, value head) units.
+    B3, T3 = 4, 4096
+    cost3 = step_bytes([0], T3, 0, T3, B3, key_heads=16, key_dim=128, value_heads=32,
+                       value_dim=128)["DeltaUpdate"]
+
+    def make_c3(whole):
+        Hk, Hv = (16, 32) if whole else (16 // N, 32 // N)
+        q, k, v, beta, decay, state = delta_inputs(torch, device, g, B3, T3, Hk, Hv, 0.0)
+        o = torch.empty_like(v)
+        ws = torch.empty(max(16, ops.delta_workspace_bytes(B3, T3, Hk, 128, Hv, 128)),
+                         dtype=torch.uint8, device=device)
+        return (lambda: ops.delta_update(q, k, v, beta, decay, state, out=o, workspace=ws)), 0
+
+    out.append(line("C3 DeltaNet prefill B=4 T=4096, 128 (sequence, value head) units in all "
+                    "(graphDeltaUpdate, chunked)",
+                    f"{128 // N} units per GPU: 4 sequences x {32 // N} value heads "
+                    f"({16 // N} key heads)", make_c3, cost3[0], reps=5, warmup=2))
+    out[-1]["tflops_cost_model"] = round(2 * cost3[1] / (out[-1]["ms"] / 1e3) / 1e12, 3)
+
+    # C4: DeltaNet recurrent step, 256 sequences.
+    cost4 = step_bytes([0], 1, 0, 1, 256, key_heads=16, key_dim=128, value_heads=32,
+                       value_dim=128)["DeltaUpdate"]
+
+    def make_c4(whole):
+        B = 256 if whole else 256 // N
+        q, k, v, beta, decay, state = delta_inputs(torch, device, g, B, 1, 16, 32, 0.02)
+        o = torch.empty_like(v)
+        return (lambda: ops.delta_update(q, k, v, beta, decay, state, out=o)), 0
+
+    out.append(line("C4 DeltaNet recurrent step, 256 sequences in all (graphDeltaUpdate)",
+                    f"{256 // N} sequences per GPU", make_c4, cost4[0]))
+    return out
+
+
 def run_secondary(torch, ops, device, peaks, dist):
     """The other kernels of the path on their benchmark configs (CUDA events, median,
     max over ranks).  Every rank runs the whole config on its own GPU, so with N GPUs
@@ -650,47 +769,12 @@ def run_secondary(torch, ops, device, peaks, dist):
                 "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4),
                 "frac_of_bf16_sustained": round(tf / peaks["bf16_tflops_sustained"], 4)})
     del q, kc, vc, out
-    # C4: DeltaNet recurrent step, B=256 per GPU.
-    B, Hk, dk, Hv, dv = 256, 16, 128, 32, 128
-    qd = torch.nn.functional.normalize(torch.randn(B, 1, Hk, dk, generator=g, device=device), dim=-1)
-    qd = (qd / dk ** 0.5).reshape(B, 1, Hk * dk).contiguous()
-    kd = torch.nn.functional.normalize(torch.randn(B, 1, Hk, dk, generator=g, device=device), dim=-1)
-    kd = kd.reshape(B, 1, Hk * dk).contiguous()
-    vd = torch.randn(B, 1, Hv * dv, generator=g, device=device).half()
-    beta = torch.sigmoid(torch.randn(B, 1, Hv, generator=g, device=device)).half().float()
-    decay = torch.exp(-torch.nn.functional.softplus(torch.randn(B, 1, Hv, generator=g, device=device)))
-    state = torch.randn(B, Hv, dk, dv, generator=g, device=device) * 0.02
-    od = torch.empty_like(vd)
-    med, best = time_op(torch, lambda: ops.delta_update(qd, kd, vd, beta, decay, state, out=od),
-                        dist)
-    nbytes = step_bytes([0], 1, 0, 1, B, key_heads=Hk, key_dim=dk, value_heads=Hv,
-                        value_dim=dv)["DeltaUpdate"][0]
-    gbs = nbytes / (med / 1e3) / 1e9
-    res.append({"workload": f"C4 DeltaNet recurrent step B=256 per GPU (graphDeltaUpdate)",
-                "ms": round(med, 4), "value": round(gbs * N, 1), "unit": "GB/s",
-                "frac_of_hbm_peak": round(gbs / peaks["hbm_gbs"], 4)})
-    del qd, kd, vd, beta, decay, state, od
-    # C3: DeltaNet prefill, B=4, T=4096 per GPU.
-    B, T = 4, 4096
-    qd = torch.nn.functional.normalize(torch.randn(B, T, Hk, dk, generator=g, device=device), dim=-1)
-    qd = (qd / dk ** 0.5).reshape(B, T, Hk * dk).contiguous()
-    kd = torch.nn.functional.normalize(torch.randn(B, T, Hk, dk, generator=g, device=device), dim=-1)
-    kd = kd.reshape(B, T, Hk * dk).contiguous()
-    vd = torch.randn(B, T, Hv * dv, generator=g, device=device).half()
-    beta = torch.sigmoid(torch.randn(B, T, Hv, generator=g, device=device)).half().float()
-    decay = torch.exp(-torch.nn.functional.softplus(torch.randn(B, T, Hv, generator=g, device=device)))
-    state = torch.zeros(B, Hv, dk, dv, device=device)
-    od = torch.empty_like(vd)
-    med, best = time_op(torch, lambda: ops.delta_update(qd, kd, vd, beta, decay, state, out=od),
-                        dist, reps=5, warmup=2)
-    cost = step_bytes([0], T, 0, T, B, key_heads=Hk, key_dim=dk, value_heads=Hv,
-                      value_dim=dv)["DeltaUpdate"]
-    gbs = cost[0] / (med / 1e3) / 1e9
-    res.append({"workload": "C3 DeltaNet prefill B=4 T=4096 per GPU (graphDeltaUpdate, chunked)",
-                "ms": round(med, 4), "value": round(gbs * N, 1), "unit": "GB/s",
-                "tflops_cost_model": round(2 * cost[1] * N / (med / 1e3) / 1e12, 3),
-                "frac_of_hbm_peak": round(gbs / peaks["hbm_gbs"], 4)})
-    del qd, kd, vd, beta, decay, state, od
+    # C2, C3 and C4 as fixed jobs split over the N GPUs (strong scaling):
+    # C2's 64 sequences, C3's 128 (sequence, value head) units as groups of
+    # whole key heads, C4's 256 sequences.  Each rank times its shard; rank 0
+    # also times the whole job alone on its GPU, which gives the efficiency
+    # t(1 GPU) / (N t(N GPUs)).
+    res.extend(run_strong(torch, ops, device, peaks, dist, g))
     # Producers at the C5 layer shapes (B=16 per GPU, T=8192): q/k RmsNorm +
     # partial RoPE of a GQA layer (k into the cache), and a DeltaNet layer's
     # conv + SiLU + q/k L2 norm and gates.  Bytes: each operand read and

@@ -152,6 +152,25 @@ int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch,
                            const float *beta, const float *decay, float *state,
                            uint16_t *out, void *stream);
 
+/* Bytes of device scratch llmi_cuda_delta_update_ws needs for this shape: 8 KB
+ * per (sequence, value head, 64-token chunk) when the call takes the
+ * chunked tensor-core form, else 0.  Same graphDeltaUpdate dispatch
+ * (MetalExecutionPlan.cpp:663-676); the scratch is this backend's own. */
+size_t llmi_cuda_delta_update_workspace(const llmi_delta_params *p, unsigned batch);
+
+/* llmi_cuda_delta_update with caller scratch: for calls of 16 or more tokens
+ * it solves every chunk's triangular system at once first (one CTA per
+ * chunk and key head, all SMs busy) and keeps only the state recurrence
+ * ordered over the chunks; same results up to rounding.  Shorter calls
+ * ignore the workspace.  workspace_bytes must be at least
+ * llmi_cuda_delta_update_workspace(p, batch), else LLMI_WORKSPACE_TOO_SMALL
+ * before any launch. */
+int llmi_cuda_delta_update_ws(const llmi_delta_params *p, unsigned batch,
+                              const float *q, const float *k, const uint16_t *v,
+                              const float *beta, const float *decay, float *state,
+                              uint16_t *out, void *workspace, size_t workspace_bytes,
+                              void *stream);
+
 /* ---- Producers of the path's operands -------------------------------------
  * The ops that turn the projections' outputs into the inputs of cacheAppend /
  * gqaFlashAttention and graphDeltaUpdate (Qwen35ModelBuilder.cpp:146-160 and

@@ -118,6 +118,10 @@ SIGNATURES = [
     ("llmi_cuda_delta_update", c_int,
      [POINTER(DeltaParams), c_uint, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
       c_void_p, c_void_p, c_void_p]),
+    ("llmi_cuda_delta_update_workspace", c_size_t, [POINTER(DeltaParams), c_uint]),
+    ("llmi_cuda_delta_update_ws", c_int,
+     [POINTER(DeltaParams), c_uint, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+      c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("llmi_cuda_norm_rope", c_int,
      [POINTER(RopeParams), c_uint, c_void_p, c_size_t, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("llmi_cuda_partial_rope", c_int,

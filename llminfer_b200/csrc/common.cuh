@@ -290,21 +290,4 @@ __device__ __forceinline__ float fast_log2(float x) {
   return y;
 }
 
-// 2^x on the FMA/ALU pipes (no MUFU), for finite x; results are meant to be
-// rounded to fp16 afterwards.  Range reduction x = n + f with n = round(x)
-// (adding 1.5*2^23 rounds to an integer held in the low mantissa bits) and
-// f in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose coefficients were
-// fitted for this library (iteratively reweighted least squares for minimum
-// relative error on [-1/2, 1/2]): max relative error 7.5e-5, below fp16's
-// 2^-11 rounding.  2^n is applied by adding n to the exponent field.  x is
-// clamped to [-125, 126] so the result stays a normal float.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fminf(fmaxf(x, -125.f), 126.f);
-  const float shifter = 12582912.f;  // 1.5 * 2^23
-  const float t = x + shifter;
-  const float f = x - (t - shifter);
-  const float p = fmaf(fmaf(fmaf(0.05517132f, f, 0.24261054f), f, 0.69326099f), f, 0.99992811f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 }  // namespace llmi

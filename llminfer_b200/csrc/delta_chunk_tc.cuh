@@ -70,8 +70,11 @@ namespace delta_tc {
 constexpr int C = 64;  // tokens per chunk
 constexpr int DK = 128, DV = 128;
 constexpr int kThreads = 256;
+// The presolved form adds a third warpgroup (warps 8-11) for the chunk's
+// inputs and outputs, so the state chain keeps only its own dependent steps.
+constexpr int kThreadsPresolved = 384;
 constexpr int kGroup = 128;            // threads per warpgroup
-constexpr int kBarLocal = 1, kBarState = 2;  // named barrier ids
+constexpr int kBarLocal = 1, kBarState = 2, kBarIO = 3;  // named barrier ids
 constexpr uint32_t kTmemCols = 512;
 // TMEM columns.  D1 and Dw share columns: D1 is read before M2 is issued.
 constexpr uint32_t kColD1 = 0, kColW = 0, kColU = 64, kColA = 128, kColY = 256, kColS = 320;
@@ -109,16 +112,21 @@ struct Smem {
   static constexpr int graw = Tu + 8192;           // fp32 decay[64], beta[64] (cp.async)
   static constexpr int gates = graw + 2 * C * 4;   // Gates[kGateSets], by chunk mod kGateSets
   static constexpr int bars = gates + kGateSets * int(sizeof(Gates));
-  static constexpr int kBars = 14;
+  static constexpr int kBars = 16;
+  // Presolved form: Am, Ad and Td are unused; their 16 KB hold the y tile
+  // the IO group stores (the fused form stores it from Vp).
+  static constexpr int YsP = Am;
   static constexpr int tmem_slot = bars + kBars * 8;
   static constexpr int abort_flag = tmem_slot + 4;
   static constexpr int total = abort_flag + 12;
 };
 static_assert(Smem::Tw % 1024 == 0 && Smem::P % 1024 == 0, "operand tiles 1024-byte aligned");
+static_assert(Smem::Tw - Smem::Am == 64 * 128 * 2, "the presolved y tile fits Am, Ad and Td");
 static_assert(sizeof(Gates) % 16 == 0, "gate sets stay 16-byte aligned");
 static_assert(Smem::total + 1024 <= 232448, "shared memory");
 
 constexpr uint32_t kVBytes = C * DV * 2, kKBytes = C * DK * 4;
+constexpr uint32_t kTuBytes = C * C * 2;  // one presolved Tu image
 
 // A tile 16x16 of a row-major fp16 [m][k] array (ldmatrix, mma.m16n8k16 layout).
 __device__ __forceinline__ void load_a(uint32_t (&f)[4], const __half *base, int ld, int m0, int k0,
@@ -163,10 +171,18 @@ __device__ __forceinline__ void load32(float (&d)[32], const float *p) {
 // (used for L2 prefetches); map_v: fp16 [batch][tokens][valueHeads * 128],
 // box 64 x 64 x 1, 128B swizzle; map_out: fp16 like v, box 128 x 64 x 1 (rows
 // past the last token are neither read - zero fill - nor written).
-__global__ void __launch_bounds__(kThreads, 1)
+//
+// Presolved: the chunk-local systems were solved beforehand for every chunk
+// at once (delta_chunk_solve.cuh); `solved` holds one 8 KB image of
+// Tu = T diag(beta) per (sequence, value head, chunk), which arrives with the
+// chunk's v boxes.  The local chain then skips A and the solve: warps 0-1
+// scale Tu's columns by e^{G_s} into Tw while warps 2-3 make P.
+template <bool Presolved>
+__global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
     chunked_tc(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                const __grid_constant__ CUtensorMap map_v,
-               const __grid_constant__ CUtensorMap map_out, const delta::Args a) {
+               const __grid_constant__ CUtensorMap map_out, const delta::Args a,
+               const uint8_t *__restrict__ solved) {
   extern __shared__ uint8_t smem_raw[];
   // Rounded up to 1024 bytes by an offset from the shared array itself, so
   // the compiler keeps every access through `smem` a shared-memory one (a
@@ -191,7 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     //     rows of the buffer's next chunk written (state -> local)
   uint64_t *bar_du = bars + 10;     // U read from TMEM (state -> local)
   uint64_t *bar_k = bars + 11;      // k rows staged (state)
-  uint64_t *bar_gates = bars + 12;  // [2] gates of the chunks of each parity (state -> local)
+  uint64_t *bar_gates = bars + 12;  // [2] gates of the chunks of each parity (state or IO -> local)
+  uint64_t *bar_m6 = bars + 14;     // presolved: M6 done (state)
+  uint64_t *bar_yread = bars + 15;  // presolved: chunk's QS and Dy read from TMEM (IO -> state)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Smem::tmem_slot);
   volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(smem + Smem::abort_flag);
   float *graw = reinterpret_cast<float *>(smem + Smem::graw);
@@ -282,6 +300,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_arrive_expect_tx(bar_k, kKBytes);
     tma_load_3d(smem + Smem::Kst, &map_k, int(kh * DK), int(chunk * C), int(seq), bar_k);
   };
+  // Staged k rows of `chunk` (fp32) into rows 0-63 of its [K; Q] buffer
+  // (fp16); every thread must have seen bar_k complete.
+  auto convert_k = [&](uint32_t chunk) {
+    uint8_t *Xb = smem + Smem::X + (chunk & 1) * 32768;
+    const float *kr = reinterpret_cast<const float *>(smem + Smem::Kst);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = gt + kGroup * i, t = idx >> 4, ch = idx & 15;
+      const float4 *k4 = reinterpret_cast<const float4 *>(kr + t * DK + 8 * ch);
+      st16(Xb + (ch >> 3) * 16384 + sw128_chunk(t, ch & 7), pack8(k4[0], k4[1]));
+    }
+    fence_proxy_async();
+  };
+  // q rows of `chunk` (fp32, global) into rows 64-127 of its [K; Q] buffer:
+  // the loads, then the fp16 stores.
+  auto load_q = [&](uint32_t chunk, float4 (&qr)[8][2]) {
+    const uint32_t t0 = chunk * C;
+    const int valid = int(min(uint32_t(C), a.tokens - t0));
+    const size_t tok0 = size_t(seq) * a.tokens + t0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = gt + kGroup * i, t = idx >> 4, ch = idx & 15;
+      if (t < valid) {
+        const float4 *src = reinterpret_cast<const float4 *>(
+            a.q + (tok0 + t) * size_t(a.key_heads) * DK + kh * DK + 8 * ch);
+        qr[i][0] = __ldg(src);
+        qr[i][1] = __ldg(src + 1);
+      } else {
+        qr[i][0] = qr[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  };
+  auto store_q = [&](uint32_t chunk, const float4 (&qr)[8][2]) {
+    uint8_t *Xb = smem + Smem::X + (chunk & 1) * 32768;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = gt + kGroup * i, t = idx >> 4, ch = idx & 15;
+      st16(Xb + (ch >> 3) * 16384 + sw128_chunk(C + t, ch & 7), pack8(qr[i][0], qr[i][1]));
+    }
+    fence_proxy_async();
+  };
   if (warp < 4) {
     // ======================= local chain (warps 0-3) =======================
     const bool elected = gt == 0;
@@ -289,10 +348,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // on the way out if the loop ends early.
     int m1_pending = -1, m23_pending = -1, v_pending = -1;
     auto issue_v = [&](uint32_t chunk) {
-      mbar_arrive_expect_tx(bar_v, kVBytes);
+      mbar_arrive_expect_tx(bar_v, Presolved ? kVBytes + kTuBytes : kVBytes);
       const int t0 = int(chunk * C);
       tma_load_3d(smem + Smem::Vraw, &map_v, int(vh * DV), t0, int(seq), bar_v);
       tma_load_3d(smem + Smem::Vraw + 8192, &map_v, int(vh * DV + 64), t0, int(seq), bar_v);
+      if (Presolved)
+        bulk_g2s(smem + Smem::Tu,
+                 solved + ((size_t(seq) * a.value_heads + vh) * n_chunks + chunk) * kTuBytes,
+                 kTuBytes, bar_v, policy_evict_first());
     };
     if (elected) {
       issue_v(0);
@@ -346,8 +409,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int hr = warp & 1;
         const int t = 32 * hr + lane;
         const float g_t = gs.g2[t], b_t = arow ? gs.bet[t] : 1.f;
+        if (Presolved && arow) {
+          // Tw = Tu diag(e^G): row t of the Tu image (loaded with the v
+          // boxes), columns scaled, into the Tw tile (same swizzled layout).
+          fail = !wait_or_abort(bar_v, n & 1, abort);
+          if (!fail) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const uint4 u = *reinterpret_cast<const uint4 *>(smem + Smem::Tu + sw128_chunk(t, c));
+              const __half2 *h2 = reinterpret_cast<const __half2 *>(&u);
+              float x[8];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(h2[e]);
+                x[2 * e] = f.x * gs.eg[8 * c + 2 * e];
+                x[2 * e + 1] = f.y * gs.eg[8 * c + 2 * e + 1];
+              }
+              st16(smem + Smem::Tw + sw128_chunk(t, c), pack8(x));
+            }
+            fence_proxy_async();
+          }
+        }
 #pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < 2 && !(Presolved && arow); ++h) {
           const int s0 = 32 * h;
           if (h > hr) {
             if (!arow) {
@@ -414,6 +498,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if constexpr (Presolved) {
+        if (named_sync_or(kBarLocal, kGroup, fail))
+          break;
+        if (elected)
+          v_pending = -1;
+      } else {
       named_sync(kBarLocal, kGroup);
 
       // L4. T = (I + A)^-1.  Diagonal blocks by column-oriented forward
@@ -516,6 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async();
       named_sync(kBarLocal, kGroup);
+      }  // !Presolved
 
       // L5. M2, M3: W^T = K^T Tw^T (K^T read MN-major from the [K; Q] tile),
       //     U^T = V^T Tu^T (V^T from the swizzled TMA boxes), once the v boxes
@@ -587,52 +678,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (v_pending >= 0)
         mbar_wait(bar_v, unsigned(v_pending));
     }
-  } else {
+  } else if constexpr (!Presolved) {
     // ======================= state chain (warps 4-7) =======================
     const bool elected = gt == 0;
     const int dv = gt;  // this thread's value column (TMEM lane)
     int m4_pending = -1, m56_pending = -1, k_pending = -1;
-    // Staged k rows of `chunk` (fp32) into rows 0-63 of its [K; Q] buffer
-    // (fp16); every thread must have seen bar_k complete.
-    auto convert_k = [&](uint32_t chunk) {
-      uint8_t *Xb = smem + Smem::X + (chunk & 1) * 32768;
-      const float *kr = reinterpret_cast<const float *>(smem + Smem::Kst);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int idx = gt + kGroup * i, t = idx >> 4, ch = idx & 15;
-        const float4 *k4 = reinterpret_cast<const float4 *>(kr + t * DK + 8 * ch);
-        st16(Xb + (ch >> 3) * 16384 + sw128_chunk(t, ch & 7), pack8(k4[0], k4[1]));
-      }
-      fence_proxy_async();
-    };
-    // q rows of `chunk` (fp32, global) into rows 64-127 of its [K; Q] buffer:
-    // the loads, then the fp16 stores.
-    auto load_q = [&](uint32_t chunk, float4 (&qr)[8][2]) {
-      const uint32_t t0 = chunk * C;
-      const int valid = int(min(uint32_t(C), a.tokens - t0));
-      const size_t tok0 = size_t(seq) * a.tokens + t0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int idx = gt + kGroup * i, t = idx >> 4, ch = idx & 15;
-        if (t < valid) {
-          const float4 *src = reinterpret_cast<const float4 *>(
-              a.q + (tok0 + t) * size_t(a.key_heads) * DK + kh * DK + 8 * ch);
-          qr[i][0] = __ldg(src);
-          qr[i][1] = __ldg(src + 1);
-        } else {
-          qr[i][0] = qr[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-    };
-    auto store_q = [&](uint32_t chunk, const float4 (&qr)[8][2]) {
-      uint8_t *Xb = smem + Smem::X + (chunk & 1) * 32768;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int idx = gt + kGroup * i, t = idx >> 4, ch = idx & 15;
-        st16(Xb + (ch >> 3) * 16384 + sw128_chunk(C + t, ch & 7), pack8(qr[i][0], qr[i][1]));
-      }
-      fence_proxy_async();
-    };
     if (elected) {
       issue_k(0);
       k_pending = 0;
@@ -886,6 +936,298 @@ __global__ void __launch_bounds__(kThreads, 1)
       bulk_wait();
     }
     if (warp == 4)
+      cp_async_wait_all();
+  } else if (warp < 8) {
+    // ============== state chain, presolved form (warps 4-7) ===============
+    // Only the steps each chunk's successor depends on: M4 (W half), V',
+    // M6, the state copy.  M4's Q half and M5 ride along for the IO group.
+    const bool elected = gt == 0;
+    const int dv = gt;
+    int m4_pending = -1, m6_pending = -1, m56_pending = -1;
+    // Initial state: S^T into TMEM in fp16 (M4's A operand) and in fp32 (the
+    // accumulator M6 adds to), the latter scaled by chunk 0's e^{G_C}, which
+    // the IO group derives first.
+    bool fail = elected && !wait_or_abort(&bar_gates[0], 0, abort);
+    const bool pro_fail = named_sync_or(kBarState, kGroup, fail);
+    if (!pro_fail) {
+      const float egl0 = gate_sets[0].egl[0];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const int key0 = 32 * q4;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          v[j] = S[(key0 + j) * DV + dv];
+        uint32_t st[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          st[j] = __float_as_uint(v[j] * egl0);
+        tmem_st32(tl + kColS + key0, st);
+        uint32_t h[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          h[j] = pack_half2(v[2 * j], v[2 * j + 1]);
+        tmem_st16(tl + kColST + 16 * q4, h);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      named_sync(kBarState, kGroup);
+    }
+    for (uint32_t n = 0; n < n_chunks && !pro_fail; ++n) {
+      const int b = n & 1;
+      const bool last = n + 1 == n_chunks;
+      const Gates &gs = gate_sets[n % kGateSets];
+      const uint32_t xs = sbase + Smem::X + b * 32768;
+
+      // P1. Chunk n's W, [K; Q], P and U are ready: M4's W half (S^T W^T),
+      //     which V' needs, then its Q half (S^T Q^T) once the IO group has
+      //     read chunk n - 1's QS from the same columns.
+      fail = !wait_or_abort(&bar_ready[b], (n >> 1) & 1, abort);
+      if (named_sync_or(kBarState, kGroup, fail))
+        break;
+      tc_fence_after();
+      if (elected) {
+        constexpr uint32_t id_w = idesc_f16(128, C, true);
+        constexpr uint32_t id_q = idesc_f16(128, C, false);
+#pragma unroll
+        for (int k = 0; k < DK / 16; ++k)
+          mma_ts(tmem + kColA, tmem + kColST + k * 8,
+                 desc_add(smem_desc(sbase + Smem::WB, 16384, 1024), k * 2048), id_w, k > 0 ? 1u : 0u);
+        mma_commit(bar_m4);
+        mma_commit(bar_wb);
+        m4_pending = int(n & 1);
+        if (n >= 1)
+          fail = !wait_or_abort(bar_yread, (n - 1) & 1, abort);
+        if (!fail) {
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < DK / 16; ++k)
+            mma_ts(tmem + kColA + C, tmem + kColST + k * 8,
+                   desc_add(smem_desc(xs, 16, 1024), (k >> 2) * 16384 + 8192 + (k & 3) * 32), id_q,
+                   k > 0 ? 1u : 0u);
+        }
+      }
+      // P2. V'^T = U^T - (W S)^T into Vp, and scaled by e^{G_C - G_t} into Vg.
+      fail = fail || !wait_or_abort(bar_m4, n & 1, abort);
+      if (named_sync_or(kBarState, kGroup, fail))
+        break;
+      m4_pending = -1;
+      tc_fence_after();
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        uint32_t u[32], w[32];
+        tmem_ld32(tl + kColU + 32 * h, u);
+        tmem_ld32(tl + kColA + 32 * h, w);
+        float ek[32];
+        load32(ek, gs.ekg + 32 * h);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float x[8], y[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            x[e] = __uint_as_float(u[8 * i + e]) - __uint_as_float(w[8 * i + e]);
+            y[e] = x[e] * ek[8 * i + e];
+          }
+          st16(smem + Smem::Vp + sw128_chunk(dv, 4 * h + i), pack8(x));
+          st16(smem + Smem::Vg + sw128_chunk(dv, 4 * h + i), pack8(y));
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      named_sync(kBarState, kGroup);
+      // P3. M6: S^T += (e^{G_C - G} V')^T K first (the next chunk waits on
+      //     it), then M5: Dy = V'^T P^T for the IO group.
+      if (elected) {
+        mbar_arrive(bar_du);
+        tc_fence_after();
+        constexpr uint32_t id5 = idesc_f16(128, C, false);
+        constexpr uint32_t id6 = idesc_f16(128, 128, true);
+#pragma unroll
+        for (int k = 0; k < C / 16; ++k)
+          mma_ss(tmem + kColS, desc_add(smem_desc(sbase + Smem::Vg, 16, 1024), k * 32),
+                 desc_add(smem_desc(xs, 16384, 1024), k * 2048), id6, 1u);
+        mma_commit(bar_m6);
+#pragma unroll
+        for (int k = 0; k < C / 16; ++k)
+          mma_ss(tmem + kColY, desc_add(smem_desc(sbase + Smem::Vp, 16, 1024), k * 32),
+                 desc_add(smem_desc(sbase + Smem::P + b * 8192, 16, 1024), k * 32), id5,
+                 k > 0 ? 1u : 0u);
+        mma_commit(bar_m56);
+        m6_pending = m56_pending = int(n & 1);
+      }
+      // P4. The state after chunk n: fp16 for the next chunk's M4 and the
+      //     fp32 accumulator scaled by the next chunk's e^{G_C} for its M6 (or,
+      //     after the last chunk, the state to memory).
+      fail = !wait_or_abort(bar_m6, n & 1, abort) ||
+             (!last && !wait_or_abort(&bar_gates[(n + 1) & 1], ((n + 1) >> 1) & 1, abort));
+      if (named_sync_or(kBarState, kGroup, fail))
+        break;
+      m6_pending = -1;
+      tc_fence_after();
+      const float egl_next = last ? 1.f : gate_sets[(n + 1) % kGateSets].egl[0];
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t v[32];
+        tmem_ld32(tl + kColS + 32 * q4, v);
+        tmem_wait_ld();
+        if (!last) {
+          uint32_t h[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            h[j] = pack_half2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+          tmem_st16(tl + kColST + 16 * q4, h);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = __float_as_uint(__uint_as_float(v[j]) * egl_next);
+          tmem_st32(tl + kColS + 32 * q4, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            S[(32 * q4 + j) * DV + dv] = __uint_as_float(v[j]);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      named_sync(kBarState, kGroup);
+    }
+    if (elected) {
+      if (m4_pending >= 0)
+        mbar_wait(bar_m4, unsigned(m4_pending));
+      if (m6_pending >= 0)
+        mbar_wait(bar_m6, unsigned(m6_pending));
+      if (m56_pending >= 0)
+        mbar_wait(bar_m56, unsigned(m56_pending));
+    }
+  } else {
+    // ================== IO group, presolved form (warps 8-11) ==================
+    // The chunk's gates, its k and q rows into [K; Q] two chunks ahead, and
+    // y = e^G (Q S) + P V' from TMEM to memory one chunk behind.
+    const bool elected = gt == 0;
+    const int dv = gt;
+    int k_pending = -1;
+    if (elected) {
+      issue_k(0);
+      k_pending = 0;
+      if (n_chunks > 2)
+        tma_prefetch_3d(&map_q, int(kh * DK), 2 * C, int(seq));
+    }
+    if (warp == 8) {
+      for (uint32_t c = 0; c < 2 && c < n_chunks; ++c) {
+        issue_gates(c);
+        gates(c);
+        if (lane == 0)
+          mbar_arrive(&bar_gates[c]);
+      }
+      if (n_chunks > 2)
+        issue_gates(2);
+    }
+    bool pro_fail = false;
+    for (uint32_t c = 0; c < 2 && c < n_chunks; ++c) {
+      float4 qr[8][2];
+      load_q(c, qr);
+      bool f = false;
+      if (elected) {
+        f = !wait_or_abort(bar_k, c & 1, abort);
+        if (!f)
+          k_pending = -1;
+      }
+      if (named_sync_or(kBarIO, kGroup, f)) {
+        pro_fail = true;
+        break;
+      }
+      convert_k(c);
+      store_q(c, qr);
+      named_sync(kBarIO, kGroup);
+      if (elected && c + 1 < n_chunks) {
+        issue_k(c + 1);
+        k_pending = int((c + 1) & 1);
+      }
+    }
+    if (elected && !pro_fail) {
+      mbar_arrive(&bar_xready[0]);
+      if (n_chunks > 1)
+        mbar_arrive(&bar_xready[1]);
+    }
+    for (uint32_t n = 0; n < n_chunks && !pro_fail; ++n) {
+      const int b = n & 1;
+      const uint32_t t0 = n * C;
+      const Gates &gs = gate_sets[n % kGateSets];
+      // Q1. Chunk n's M4 (Q half), M5 and M6 are done; the previous output
+      //     tile has left shared memory.
+      if (elected)
+        bulk_wait_read();
+      bool fail = !wait_or_abort(bar_m56, n & 1, abort);
+      if (named_sync_or(kBarIO, kGroup, fail))
+        break;
+      tc_fence_after();
+      float4 qr[8][2];
+      const bool q_next = n + 2 < n_chunks;
+      if (q_next)
+        load_q(n + 2, qr);
+      if (elected && n + 3 < n_chunks)
+        tma_prefetch_3d(&map_q, int(kh * DK), int(t0 + 3 * C), int(seq));
+      // Q2. y^T = e^G (Q S)^T + Dy into the output tile, then to memory.
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        uint32_t ya[32], yd[32];
+        tmem_ld32(tl + kColA + C + 32 * h, ya);
+        tmem_ld32(tl + kColY + 32 * h, yd);
+        float e[32];
+        load32(e, gs.eg + 32 * h);
+        tmem_wait_ld();
+        __half *ys = reinterpret_cast<__half *>(smem + Smem::YsP) + dv;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          ys[(32 * h + j) * DV] =
+              __float2half_rn(fmaf(e[j], __uint_as_float(ya[j]), __uint_as_float(yd[j])));
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      named_sync(kBarIO, kGroup);
+      if (elected) {
+        mbar_arrive(bar_yread);
+        tma_store_3d(&map_out, smem + Smem::YsP, int(vh * DV), int(t0), int(seq));
+        bulk_commit();
+      }
+      // Q3. [K; Q] buffer b is free: chunk n + 2's k and q rows into it;
+      //     the staging tile then takes chunk n + 3's k rows.
+      if (q_next) {
+        fail = false;
+        if (elected) {
+          fail = !wait_or_abort(bar_k, n & 1, abort);
+          if (!fail)
+            k_pending = -1;
+        }
+        if (named_sync_or(kBarIO, kGroup, fail))
+          break;
+        convert_k(n + 2);
+        store_q(n + 2, qr);
+        named_sync(kBarIO, kGroup);
+        if (elected) {
+          if (n + 3 < n_chunks) {
+            issue_k(n + 3);
+            k_pending = int((n + 3) & 1);
+          }
+          mbar_arrive(&bar_xready[b]);
+        }
+      }
+      // Q4. Gates of chunk n + 2, which the local chain reads at its step L3
+      //     and the state chain at the end of chunk n + 1.
+      if (warp == 8 && n + 2 < n_chunks) {
+        gates(n + 2);
+        if (n + 3 < n_chunks)
+          issue_gates(n + 3);
+        if (lane == 0)
+          mbar_arrive(&bar_gates[n & 1]);
+      }
+    }
+    if (elected) {
+      if (k_pending >= 0)
+        mbar_wait(bar_k, unsigned(k_pending));
+      bulk_wait();
+    }
+    if (warp == 8)
       cp_async_wait_all();
   }
 

@@ -10,6 +10,7 @@
 
 #include "cache_append.cuh"
 #include "common.cuh"
+#include "delta_chunk_solve.cuh"
 #include "delta_chunk_tc.cuh"
 #include "delta_recurrent.cuh"
 #include "gqa_decode.cuh"
@@ -353,20 +354,21 @@ bool prefill_tc_fits(const llmi_gqa_params &p, unsigned batch, const void *q, co
          p.kvHeads <= 65535;
 }
 
-int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *q,
-                      const uint16_t *k, const uint16_t *v, size_t cache_stride, uint16_t *out,
-                      const DeviceInfo &dev, cudaStream_t stream) {
+// The prefill's tensor maps.  caches [batch][rows][Hkv][D] at sequence
+// stride cache_stride: single CTAs stage K boxes of 64 dims x 1 head x 128
+// keys and V boxes of 32 keys; each CTA of a pair stages K boxes of 64 keys
+// and V boxes of 128 keys.  q [batch][tokens][Hq][D]: a box is the CTA's 128
+// rows (G heads x 128/G tokens) x 64 dims, rows in (token, head) order.
+int encode_prefill_maps(const llmi_gqa_params &p, unsigned batch, const uint16_t *q,
+                        const uint16_t *k, const uint16_t *v, size_t cache_stride, bool pairs,
+                        CUtensorMap &mq, CUtensorMap &mk, CUtensorMap &mv) {
   using namespace prefill_tc;
   const uint32_t G = p.queryHeads / p.kvHeads;
   const uint32_t rows = p.past + p.tokens;
   const uint64_t D = kD;
-  CUtensorMap mq, mk, mv;
-  const bool pairs = prefill_on_pairs();
-  // caches [batch][rows][Hkv][D] at sequence stride cache_stride.  Single
-  // CTAs stage K boxes of 64 dims x 1 head x 128 keys and V boxes of 32 keys;
-  // each CTA of a pair stages K boxes of 64 keys and V boxes of 128 keys.
   {
-    const uint64_t seq_bytes = batch > 1 ? uint64_t(cache_stride) * 2 : uint64_t(rows) * p.kvHeads * D * 2;
+    const uint64_t seq_bytes =
+        batch > 1 ? uint64_t(cache_stride) * 2 : uint64_t(rows) * p.kvHeads * D * 2;
     const uint64_t dims[4] = {D, p.kvHeads, rows, batch};
     const uint64_t strides[3] = {D * 2, uint64_t(p.kvHeads) * D * 2, seq_bytes};
     const uint32_t kbox[4] = {64, 1, uint32_t(pairs ? prefill_tc2::kHalfKeys : kKeys), 1};
@@ -376,15 +378,73 @@ int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *
     if (int s = encode_map_4d(&mv, v, dims, strides, vbox))
       return s;
   }
-  // q [batch][tokens][Hq][D]: a box is the CTA's 128 rows (G heads x 128/G
-  // tokens) x 64 dims, rows in (token, head) order.
-  {
-    const uint64_t dims[4] = {D, p.queryHeads, p.tokens, batch};
-    const uint64_t strides[3] = {D * 2, uint64_t(p.queryHeads) * D * 2,
-                                 uint64_t(p.tokens) * p.queryHeads * D * 2};
-    const uint32_t box[4] = {64, G, uint32_t(kRows) / G, 1};
-    if (int s = encode_map_4d(&mq, q, dims, strides, box))
+  const uint64_t dims[4] = {D, p.queryHeads, p.tokens, batch};
+  const uint64_t strides[3] = {D * 2, uint64_t(p.queryHeads) * D * 2,
+                               uint64_t(p.tokens) * p.queryHeads * D * 2};
+  const uint32_t box[4] = {64, G, uint32_t(kRows) / G, 1};
+  return encode_map_4d(&mq, q, dims, strides, box);
+}
+
+// The prefill's three tensor maps for one call's operands.  Encoding them
+// costs the host several microseconds per call, which dominates short
+// prefills, so each thread keeps the maps of its last few distinct calls
+// (same pointers, shape and cache stride: a serving loop or a replayed
+// capture repeats them) and reuses them.
+struct PrefillMaps {
+  const void *q, *k, *v;
+  int device;
+  uint32_t tokens, past, query_heads, kv_heads;
+  unsigned batch;
+  size_t cache_stride;
+  bool pairs;
+  CUtensorMap mq, mk, mv;
+
+  bool same(const PrefillMaps &o) const {
+    return q == o.q && k == o.k && v == o.v && device == o.device && tokens == o.tokens &&
+           past == o.past && query_heads == o.query_heads && kv_heads == o.kv_heads &&
+           batch == o.batch && cache_stride == o.cache_stride && pairs == o.pairs;
+  }
+};
+
+int launch_prefill_tc(const llmi_gqa_params &p, unsigned batch, const uint16_t *q,
+                      const uint16_t *k, const uint16_t *v, size_t cache_stride, uint16_t *out,
+                      const DeviceInfo &dev, cudaStream_t stream) {
+  using namespace prefill_tc;
+  const uint32_t G = p.queryHeads / p.kvHeads;
+  const bool pairs = prefill_on_pairs();
+  constexpr int kCached = 8;
+  thread_local PrefillMaps cache[kCached];
+  thread_local int cached = 0, next_slot = 0;
+  PrefillMaps key{};
+  key.q = q;
+  key.k = k;
+  key.v = v;
+  key.device = dev.device;
+  key.tokens = p.tokens;
+  key.past = p.past;
+  key.query_heads = p.queryHeads;
+  key.kv_heads = p.kvHeads;
+  key.batch = batch;
+  key.cache_stride = batch > 1 ? cache_stride : 0;
+  key.pairs = pairs;
+  const PrefillMaps *hit = nullptr;
+  for (int i = 0; i < cached && !hit; ++i)
+    if (cache[i].same(key))
+      hit = &cache[i];
+  CUtensorMap mq, mk, mv;
+  if (hit) {
+    mq = hit->mq;
+    mk = hit->mk;
+    mv = hit->mv;
+  } else {
+    if (int s = encode_prefill_maps(p, batch, q, k, v, cache_stride, pairs, mq, mk, mv))
       return s;
+    key.mq = mq;
+    key.mk = mk;
+    key.mv = mv;
+    cache[next_slot] = key;
+    next_slot = (next_slot + 1) % kCached;
+    cached = std::min(cached + 1, kCached);
   }
   Args a;
   a.out = reinterpret_cast<__half *>(out);
@@ -679,10 +739,63 @@ extern "C" int llmi_cuda_gqa_decode_noalloc(const llmi_gqa_params *p, unsigned b
 
 // ---- graphDeltaUpdate ----------------------------------------------------------------
 
+namespace {
+
+// The chunked tensor-core form applies (tokens >= kChunkedMinTokens, 128 x 128
+// heads, 16-byte aligned operands).
+bool delta_chunked(const llmi_delta_params *p, unsigned batch, const void *q, const void *k,
+                   const void *v, const void *state, const void *out) {
+  return p->tokens >= kChunkedMinTokens && p->keyDim == 128 && p->valueDim == 128 &&
+         aligned16(q) && aligned16(k) && aligned16(v) && aligned16(state) && aligned16(out) &&
+         batch <= 65535 && p->valueHeads <= 2147483647u && p->keyHeads <= 65535;
+}
+
+size_t delta_solved_bytes(const llmi_delta_params *p, unsigned batch) {
+  const uint64_t chunks = (uint64_t(p->tokens) + delta_tc::C - 1) / delta_tc::C;
+  return size_t(uint64_t(batch) * p->valueHeads * chunks * delta_tc::kTuBytes);
+}
+
+int delta_update_impl(const llmi_delta_params *p, unsigned batch, const float *q, const float *k,
+                      const uint16_t *v, const float *beta, const float *decay, float *state,
+                      uint16_t *out, void *workspace, size_t workspace_bytes, bool with_ws,
+                      void *stream);
+
+}  // namespace
+
+extern "C" size_t llmi_cuda_delta_update_workspace(const llmi_delta_params *p, unsigned batch) {
+  clear_error();
+  if (!p || !batch || !p->tokens || !p->keyHeads || !p->valueHeads) {
+    fail(LLMI_INVALID_ARGUMENT, "DeltaUpdate workspace: null parameters or zero sizes");
+    return 0;
+  }
+  // Alignment is the caller's; size as if the chunked form applies.
+  if (p->tokens < kChunkedMinTokens || p->keyDim != 128 || p->valueDim != 128)
+    return 0;
+  return delta_solved_bytes(p, batch);
+}
+
 extern "C" int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch, const float *q,
                                       const float *k, const uint16_t *v, const float *beta,
                                       const float *decay, float *state, uint16_t *out,
                                       void *stream) {
+  return delta_update_impl(p, batch, q, k, v, beta, decay, state, out, nullptr, 0, false, stream);
+}
+
+extern "C" int llmi_cuda_delta_update_ws(const llmi_delta_params *p, unsigned batch,
+                                         const float *q, const float *k, const uint16_t *v,
+                                         const float *beta, const float *decay, float *state,
+                                         uint16_t *out, void *workspace, size_t workspace_bytes,
+                                         void *stream) {
+  return delta_update_impl(p, batch, q, k, v, beta, decay, state, out, workspace,
+                           workspace_bytes, true, stream);
+}
+
+namespace {
+
+int delta_update_impl(const llmi_delta_params *p, unsigned batch, const float *q, const float *k,
+                      const uint16_t *v, const float *beta, const float *decay, float *state,
+                      uint16_t *out, void *workspace, size_t workspace_bytes, bool with_ws,
+                      void *stream) {
   clear_error();
   if (!p || !q || !k || !v || !beta || !decay || !state || !out)
     return fail(LLMI_INVALID_ARGUMENT, "DeltaUpdate: null parameter or tensor pointer");
@@ -708,10 +821,17 @@ extern "C" int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch
   a.group = p->valueHeads / p->keyHeads;
   cudaStream_t s = as_stream(stream);
   // Multi-token calls: chunked form on tensor cores (dk = dv = 128).
-  const bool chunked = p->tokens >= kChunkedMinTokens && p->keyDim == 128 && p->valueDim == 128 &&
-                       aligned16(q) && aligned16(k) && aligned16(v) && aligned16(state) &&
-                       aligned16(out) && batch <= 65535 && p->valueHeads <= 2147483647u;
+  const bool chunked = delta_chunked(p, batch, q, k, v, state, out);
   if (chunked) {
+    const bool presolve = with_ws;
+    if (presolve) {
+      const size_t need = delta_solved_bytes(p, batch);
+      if (workspace_bytes < need || !workspace || !aligned16(workspace))
+        return fail(LLMI_WORKSPACE_TOO_SMALL,
+                    "DeltaUpdate: workspace of %zu B at %p; this shape needs %zu B, 16-byte "
+                    "aligned (llmi_cuda_delta_update_workspace)",
+                    workspace_bytes, workspace, need);
+    }
     DeviceInfo dev;
     if (int e = current_device(dev))
       return e;
@@ -744,10 +864,28 @@ extern "C" int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch
         return e;
     }
     const size_t smem = delta_tc::Smem::total + 1024;
-    if (int e = allow_smem(reinterpret_cast<const void *>(delta_tc::chunked_tc), smem, dev))
-      return e;
     dim3 grid(p->valueHeads, batch);
-    delta_tc::chunked_tc<<<grid, delta_tc::kThreads, smem, s>>>(mq, mk, mv, mo, a);
+    if (presolve) {
+      // Every chunk's triangular system at once, then the state recurrence.
+      const size_t solve_smem = sizeof(delta_solve::Smem);
+      if (int e = allow_smem(reinterpret_cast<const void *>(delta_solve::solve_pass), solve_smem,
+                             dev))
+        return e;
+      if (int e = allow_smem(reinterpret_cast<const void *>(delta_tc::chunked_tc<true>), smem, dev))
+        return e;
+      const uint32_t chunks = (p->tokens + delta_tc::C - 1) / delta_tc::C;
+      uint8_t *solved = static_cast<uint8_t *>(workspace);
+      delta_solve::solve_pass<<<dim3(chunks, p->keyHeads, batch), delta_solve::kThreads,
+                                solve_smem, s>>>(a, solved);
+      if (int e = launched("graphDeltaUpdate (chunk systems)"))
+        return e;
+      delta_tc::chunked_tc<true><<<grid, delta_tc::kThreadsPresolved, smem, s>>>(mq, mk, mv, mo, a,
+                                                                                solved);
+      return launched("graphDeltaUpdate (chunked, presolved, tcgen05)");
+    }
+    if (int e = allow_smem(reinterpret_cast<const void *>(delta_tc::chunked_tc<false>), smem, dev))
+      return e;
+    delta_tc::chunked_tc<false><<<grid, delta_tc::kThreads, smem, s>>>(mq, mk, mv, mo, a, nullptr);
     return launched("graphDeltaUpdate (chunked, tcgen05)");
   }
   const bool fast = p->valueDim == 128 && (p->keyDim == 128 || p->keyDim == 64) &&
@@ -772,6 +910,8 @@ extern "C" int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch
   return launch_dependent("graphDeltaUpdate (recurrent, generic)", delta::recurrent_generic,
                           dim3(uint32_t((columns + 127) / 128)), 128, 0, s, a);
 }
+
+}  // namespace
 
 // ---- device error word ---------------------------------------------------------------
 

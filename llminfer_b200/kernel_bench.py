@@ -10,6 +10,7 @@ on the CPU before timing).  Prints one JSON object.
   python -m llminfer_b200.kernel_bench decode  --batch 64 --past 4096 --capacity 8192
   python -m llminfer_b200.kernel_bench prefill --batch 1 --tokens 128
   python -m llminfer_b200.kernel_bench delta   --batch 256 --tokens 1 --state-std 0.02
+  python -m llminfer_b200.kernel_bench delta   --batch 4 --tokens 4096 [--no-scratch]
   python -m llminfer_b200.kernel_bench append  --batch 64 --tokens 1 --past 4096
   python -m llminfer_b200.kernel_bench rope    --batch 16 --tokens 8192 --past 0
   python -m llminfer_b200.kernel_bench deltaprep --batch 16 --tokens 8192
@@ -121,7 +122,12 @@ def bench_delta(args):
     state0 = torch.randn(B, Hv, dk, dv, generator=gen, device="cuda") * args.state_std
     state = state0.clone()
     out = torch.empty_like(v)
-    fn = lambda: ops.delta_update(q, k, v, beta, decay, state, out=out)
+    if args.no_scratch:
+        ws = False  # llmi_cuda_delta_update: one kernel per head, no scratch
+    else:
+        ws = torch.empty(max(16, ops.delta_workspace_bytes(B, T, Hk, dk, Hv, dv)),
+                         dtype=torch.uint8, device="cuda")
+    fn = lambda: ops.delta_update(q, k, v, beta, decay, state, out=out, workspace=ws)
     check = None
     if not args.no_check:
         fn()
@@ -146,7 +152,8 @@ def bench_delta(args):
     nbytes = B * (2 * T * Hk * dk * 4 + T * Hv * dv * 2 + 2 * T * Hv * 4 + 2 * Hv * dk * dv * 4
                   + T * Hv * dv * 2)
     hbm, tf, src = peaks()
-    return dict(op="graphDeltaUpdate", batch=B, tokens=T, heads=[Hk, Hv], dims=[dk, dv],
+    return dict(op="graphDeltaUpdate", form="no scratch" if args.no_scratch else "scratch",
+                batch=B, tokens=T, heads=[Hk, Hv], dims=[dk, dv],
                 best_ms=best, median_ms=med, gbs=nbytes / (med * 1e-3) / 1e9,
                 hbm_frac=nbytes / (med * 1e-3) / 1e9 / hbm,
                 cost_model_tflops=2 * 3 * B * T * Hv * dk * dv / (med * 1e-3) / 1e12,
@@ -267,6 +274,8 @@ def main(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--seed", type=int, default=179531)
     p.add_argument("--no-check", action="store_true")
+    p.add_argument("--no-scratch", action="store_true",
+                   help="delta: the entry point without scratch (llmi_cuda_delta_update)")
     args = p.parse_args(argv)
     torch.cuda.set_device(0)
     if args.op == "decode":

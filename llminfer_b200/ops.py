@@ -99,10 +99,23 @@ def gqa_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pa
     return out
 
 
+def delta_workspace_bytes(batch: int, tokens: int, key_heads: int, key_dim: int,
+                          value_heads: int, value_dim: int) -> int:
+    """Scratch bytes of delta_update's chunk-parallel form (0 if the call does not use it)."""
+    p = abi.DeltaParams(tokens, key_heads, key_dim, value_heads, value_dim)
+    return lib.llmi_cuda_delta_update_workspace(ctypes.byref(p), batch)
+
+
 def delta_update(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
                  decay: torch.Tensor, state: torch.Tensor, out: torch.Tensor | None = None,
+                 workspace: torch.Tensor | bool | None = None,
                  stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-    """graphDeltaUpdate: updates state [B, Hv, dk, dv] in place, returns out [B, T, Hv*dv]."""
+    """graphDeltaUpdate: updates state [B, Hv, dk, dv] in place, returns out [B, T, Hv*dv].
+
+    workspace None allocates the scratch of the chunk-parallel form
+    (llmi_cuda_delta_update_ws); a uint8 tensor is used as that scratch;
+    False calls llmi_cuda_delta_update, which takes no scratch (one kernel
+    walks each head's chunks and solves their systems in order)."""
     for t, n in ((q, "q"), (k, "k"), (beta, "beta"), (decay, "decay"), (state, "state")):
         _need(t, torch.float32, n)
     _need(v, torch.float16, "v")
@@ -111,9 +124,18 @@ def delta_update(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.
     p = abi.DeltaParams(T, key_width // dk, dk, Hv, dv)
     out = torch.empty_like(v) if out is None else out
     _need(out, torch.float16, "out")
-    check(lib.llmi_cuda_delta_update(ctypes.byref(p), B, q.data_ptr(), k.data_ptr(),
-                                     v.data_ptr(), beta.data_ptr(), decay.data_ptr(),
-                                     state.data_ptr(), out.data_ptr(), _stream(stream)))
+    if workspace is False:
+        check(lib.llmi_cuda_delta_update(ctypes.byref(p), B, q.data_ptr(), k.data_ptr(),
+                                         v.data_ptr(), beta.data_ptr(), decay.data_ptr(),
+                                         state.data_ptr(), out.data_ptr(), _stream(stream)))
+        return out
+    if workspace is None:
+        n = lib.llmi_cuda_delta_update_workspace(ctypes.byref(p), B)
+        workspace = torch.empty(max(n, 16), dtype=torch.uint8, device=q.device)
+    check(lib.llmi_cuda_delta_update_ws(ctypes.byref(p), B, q.data_ptr(), k.data_ptr(),
+                                        v.data_ptr(), beta.data_ptr(), decay.data_ptr(),
+                                        state.data_ptr(), out.data_ptr(), workspace.data_ptr(),
+                                        workspace.numel(), _stream(stream)))
     return out
 
 

@@ -36,11 +36,11 @@ def report(name, got, want):
     assert max_abs <= _inputs.MAX_ABS and rel <= _inputs.REL_L2, (name, max_abs, rel)
 
 
-def run_delta(case):
+def run_delta(case, workspace):
     state = dev(case["state"])
     out = torch.full(case["v"].shape, float("nan"), dtype=torch.float16, device="cuda")
     ops.delta_update(dev(case["q"]), dev(case["k"]), dev(case["v"]), dev(case["beta"]),
-                     dev(case["decay"]), state, out=out)
+                     dev(case["decay"]), state, out=out, workspace=workspace)
     torch.cuda.synchronize()
     return out.float().cpu().numpy(), state.cpu().numpy()
 
@@ -52,11 +52,15 @@ def run_delta(case):
 ])
 def test_delta_at_benchmark_size(name, batch, tokens, std):
     case = _inputs.delta_case(batch, tokens, 16, 128, 32, 128, state_std=std, seed=41)
-    got_out, got_state = run_delta(case)
     want_out, want_state = _oracle.delta_update(case["q"], case["k"], case["v"], case["beta"],
                                                 case["decay"], case["state"])
-    report(name + " output", got_out, want_out)
-    report(name + " state", got_state, want_state)
+    # Both entry points: with scratch (chunk systems solved in parallel, the
+    # form the benchmark runs) and without (one kernel per head).
+    forms = (("", None), (" [no scratch]", False)) if tokens > 1 else (("", None),)
+    for tag, ws in forms:
+        got_out, got_state = run_delta(case, ws)
+        report(name + tag + " output", got_out, want_out)
+        report(name + tag + " state", got_state, want_state)
 
 
 def test_decode_c2_full_batch():

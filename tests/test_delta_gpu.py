@@ -9,7 +9,7 @@ import torch
 
 import _inputs
 import _oracle
-from llminfer_b200 import ops
+from llminfer_b200 import abi, ops
 
 pytestmark = pytest.mark.gpu
 
@@ -20,11 +20,17 @@ def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-def run(case):
+# The two entry points: llmi_cuda_delta_update_ws (chunk systems solved for
+# every chunk at once, then the state pass) and llmi_cuda_delta_update (one
+# kernel per head that solves each chunk's system in order, no scratch).
+FORMS = {"presolved": None, "fused": False}
+
+
+def run(case, form="presolved"):
     state = dev(case["state"])
     out = torch.full(case["v"].shape, float("nan"), dtype=torch.float16, device="cuda")
     ops.delta_update(dev(case["q"]), dev(case["k"]), dev(case["v"]), dev(case["beta"]),
-                     dev(case["decay"]), state, out=out)
+                     dev(case["decay"]), state, out=out, workspace=FORMS[form])
     torch.cuda.synchronize()
     return out.float().cpu().numpy(), state.cpu().numpy()
 
@@ -53,22 +59,47 @@ def check(case, got_out, got_state):
     (2, 3, 2, 7, 4, 5, 0.02),         # odd dims (generic kernel)
     (1, 130, 2, 16, 4, 8, 0.02),
 ])
-def test_delta_matches_oracle(batch, tokens, hk, dk, hv, dv, std):
+@pytest.mark.parametrize("form", sorted(FORMS))
+def test_delta_matches_oracle(batch, tokens, hk, dk, hv, dv, std, form):
     case = _inputs.delta_case(batch, tokens, hk, dk, hv, dv, state_std=std, seed=31 + tokens)
-    check(case, *run(case))
+    check(case, *run(case, form))
 
 
-def test_delta_prefill_config_reduced():
+@pytest.mark.parametrize("form", sorted(FORMS))
+def test_delta_prefill_config_reduced(form):
     # C3 per-sequence shape (16 key heads, 32 value heads, 128 x 128), shorter.
     case = _inputs.delta_case(1, 256, 16, 128, 32, 128, seed=33)
-    check(case, *run(case))
+    check(case, *run(case, form))
 
 
-def test_delta_matches_transformers_fixture():
+@pytest.mark.parametrize("hk,hv", [(4, 4), (2, 8), (1, 3)])
+def test_presolved_groups(hk, hv):
+    # Key heads shared by 1, 4 and 3 value heads: the solve pass walks the
+    # value heads of its key head; ragged last chunk, a decay of exactly 0.
+    case = _inputs.delta_case(2, 150, hk, 128, hv, 128, state_std=0.02, seed=hv)
+    case["decay"][1, 70, 0] = 0.0
+    check(case, *run(case, "presolved"))
+    check(case, *run(case, "fused"))
+
+
+def test_presolved_rejects_small_workspace():
+    case = _inputs.delta_case(1, 64, 1, 128, 2, 128, seed=3)
+    small = torch.empty(8192, dtype=torch.uint8, device="cuda")  # needs 2 x 8 KB
+    out = torch.full(case["v"].shape, float("nan"), dtype=torch.float16, device="cuda")
+    with pytest.raises(abi.LlmiError) as err:
+        ops.delta_update(dev(case["q"]), dev(case["k"]), dev(case["v"]), dev(case["beta"]),
+                         dev(case["decay"]), dev(case["state"]), out=out, workspace=small)
+    assert err.value.status == abi.LLMI_WORKSPACE_TOO_SMALL
+    torch.cuda.synchronize()
+    assert torch.isnan(out).all()
+
+
+@pytest.mark.parametrize("form", sorted(FORMS))
+def test_delta_matches_transformers_fixture(form):
     d = np.load(GOLDEN / "delta_xcheck.npz")
     case = dict(q=d["q"], k=d["k"], v=d["v"].view(np.float16), beta=d["beta"],
                 decay=d["decay"], state=d["state"])
-    out, state = run(case)
+    out, state = run(case, form)
     max_abs, rel = _inputs.errors(out, d["recurrent_out"])
     assert max_abs <= _inputs.MAX_ABS and rel <= _inputs.REL_L2, (max_abs, rel)
     max_abs, rel = _inputs.errors(state, d["recurrent_state"])
