@@ -513,17 +513,26 @@ def run_ours(args, dist):
             tag = entry["workload"].split(" ")[0]
             if tag in cpu_ops:
                 entry["cpu_baseline"] = cpu_ops[tag]
-    stack = None
+    stack = stack_seq = None
     if not args.no_stack:
         from llminfer_b200.stack import run_stack
-        dist.barrier()
-        stack = run_stack(torch, dist.pg, dist.world, dist.rank, **C5)
-        stack["prefill_frac_of_bf16_peak"] = round(
-            stack["prefill_tflops"] / dist.world / peaks["bf16_tflops"], 4)
-        stack["decode_frac_of_hbm_peak"] = round(
-            stack["decode_gbs"] / dist.world / peaks["hbm_gbs"], 4)
-        stack["scaling"] = "strong"
-        torch.cuda.empty_cache()
+
+        def one_stack(split):
+            dist.barrier()
+            r = run_stack(torch, dist.pg, dist.world, dist.rank, split=split, **C5)
+            r["prefill_frac_of_bf16_peak"] = round(
+                r["prefill_tflops"] / dist.world / peaks["bf16_tflops"], 4)
+            r["decode_frac_of_hbm_peak"] = round(
+                r["decode_gbs"] / dist.world / peaks["hbm_gbs"], 4)
+            r["scaling"] = "strong"
+            torch.cuda.empty_cache()
+            return r
+
+        # The config's (sequence x head) sharding with its all-gathers, and
+        # beside it (N > 1) whole sequences per GPU, which needs no collective.
+        stack = one_stack("heads")
+        if dist.world > 1:
+            stack_seq = one_stack("sequences")
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": dist.world,
@@ -557,6 +566,7 @@ def run_ours(args, dist):
         "clocks": clocks.summary(),
         "secondary": secondary,
         "stack": stack,
+        "stack_sequence_major": stack_seq,
     }
     return line
 

@@ -198,6 +198,15 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
     if (int e = ensure_workspace(s, need))
       return e;
   }
+  // Multi-token DeltaNet steps solve every chunk's system first, into the
+  // same workspace (a step has either a decode or a chunked DeltaUpdate
+  // need, never both); it grows to the longest prefill step seen.
+  if (tokens > 1 && c.hasDelta()) {
+    llmi_delta_params d{tokens, c.keyHeads, c.keyDim, c.valueHeads, c.valueDim};
+    if (const size_t need = llmi_cuda_delta_update_workspace(&d, B))
+      if (int e = ensure_workspace(s, need))
+        return e;
+  }
   const size_t cacheStride = size_t(c.capacity) * c.kvHeads * c.headDim;
   const auto dispatches = lower(graph);
   size_t next = 0;  // first dispatch of the current op
@@ -325,11 +334,12 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
     case OpKind::DeltaUpdate: {
       llmi_delta_params p{tokens, c.keyHeads, c.keyDim, c.valueHeads, c.valueDim};
       launchedAny = true;
-      e = llmi_cuda_delta_update(&p, B, static_cast<const float *>(x.q),
-                                 static_cast<const float *>(x.k),
-                                 static_cast<const uint16_t *>(x.v), x.beta, x.decay,
-                                 static_cast<float *>(s.recurrent[op.layer]),
-                                 static_cast<uint16_t *>(x.out), s.stream);
+      e = llmi_cuda_delta_update_ws(&p, B, static_cast<const float *>(x.q),
+                                    static_cast<const float *>(x.k),
+                                    static_cast<const uint16_t *>(x.v), x.beta, x.decay,
+                                    static_cast<float *>(s.recurrent[op.layer]),
+                                    static_cast<uint16_t *>(x.out), s.workspace,
+                                    s.workspaceBytes, s.stream);
       break;
     }
     }

@@ -12,9 +12,11 @@ with q scaled by 1/sqrt(dk), v ~ N(0,1) fp16, beta = half(sigmoid(N(0,1))),
 decay = exp(-softplus(N(0,1)))); two operand sets per layer kind alternate
 between layers, so consecutive layers never read the same buffers.
 
-One process per GPU.  The (sequence x head) units are split as N = Ns x Nh:
-Nh head groups (the largest divisor of N that divides every head count) and
-Ns = N / Nh sequence groups.  Rank r owns sequence group r // Nh and head
+One process per GPU.  The (sequence x head) units are split as N = Ns x Nh.
+The config's head sharding ("heads") takes Nh head groups (the largest
+divisor of N that divides every head count) and Ns = N / Nh sequence groups;
+the sequence-major split ("sequences") gives every rank whole sequences
+(Nh = 1), so no collective is needed at all.  Rank r owns sequence group r // Nh and head
 group r % Nh and opens an AttentionSession over that shard (B/Ns sequences,
 H/Nh of every head count; head group g of the GQA layers holds query heads
 [g Hq/Nh, (g+1) Hq/Nh) and their KV heads, of the DeltaNet layers value heads
@@ -56,9 +58,19 @@ class ShardPlan:
     head_groups: int
 
     @classmethod
-    def make(cls, world: int, rank: int, batch: int, shape: dict) -> "ShardPlan":
+    def make(cls, world: int, rank: int, batch: int, shape: dict,
+             split: str = "heads") -> "ShardPlan":
+        """split "heads": as many head groups as divide every head count (the
+        config's head sharding, with a collective per layer); "sequences":
+        whole sequences per rank (Nh = 1), no collective."""
         if not 0 <= rank < world:
             raise ValueError(f"rank {rank} outside world {world}")
+        if split == "sequences":
+            if batch % world:
+                raise ValueError(f"batch {batch} does not split over {world} ranks")
+            return cls(world, rank, world, 1)
+        if split != "heads":
+            raise ValueError(f"unknown split {split!r}")
         g = 0
         for h in ("query_heads", "kv_heads", "key_heads", "value_heads"):
             g = math.gcd(g, shape[h])
@@ -221,8 +233,10 @@ class StackRun:
         self.graphs = None  # per decode step, once capture_decode() has run
         n = plan.world
         # Without a process group (dist None) a multi-rank plan runs one
-        # shard on this GPU and leaves the outputs unshared (emulation).
-        self.gathering = dist is not None and n > 1
+        # shard on this GPU and leaves the outputs unshared (emulation).  A
+        # sequence-major split needs no collective: every rank holds all heads
+        # of its sequences.
+        self.gathering = dist is not None and n > 1 and plan.head_groups > 1
         self.pre_gathered = self.dec_gathered = None
         if self.gathering:
             self.pre_gathered = torch.empty(n, self.b, prefill, self.width, dtype=torch.float16,
@@ -271,12 +285,13 @@ class StackRun:
         torch = self.torch
         buf = step & 1
         out = self.dec_out[buf]
-        self.stream.wait_event(self.dec_free[buf])
         if self.graphs is not None:
+            # The step's launches and its all-gather are one graph.
             with torch.cuda.stream(self.stream):
                 self.graphs[step].replay()
-        else:
-            self.session.enqueue(1, self._dec_tables[buf])
+            return
+        self.stream.wait_event(self.dec_free[buf])
+        self.session.enqueue(1, self._dec_tables[buf])
         if self.gathering:
             self.step_done.record(self.stream)
             self.comm.wait_event(self.step_done)
@@ -284,12 +299,16 @@ class StackRun:
         self.dec_free[buf].record(self.comm)
 
     def capture_decode(self):
-        """Captures each decode step's launches into its own CUDA graph (the
-        step's `past` is part of its kernel arguments), so a step costs one
-        graph launch on the host instead of ~2 launches per layer.  Call right
-        after a prefill: capturing runs nothing on the GPU but advances the
-        session's `past` through every decode step, so reset the session and
-        run the prefill again before replaying with run_decode_step."""
+        """Captures each decode step into its own CUDA graph (the step's `past`
+        is part of its kernel arguments): the session's launches and, when the
+        heads are sharded, the NCCL all-gather of the step's head outputs on
+        the comm stream, joined back before the graph ends.  A step then costs
+        the host one graph launch, with no per-step collective call from
+        Python.  Every rank captures the same collectives in the same order.
+        Call right after a prefill (the communicator exists by then):
+        capturing runs nothing on the GPU but advances the session's `past`
+        through every decode step, so reset the session and run the prefill
+        again before replaying with run_decode_step."""
         torch = self.torch
         if self.session.past != self.prefill:
             raise RuntimeError("capture_decode needs the session right after a prefill")
@@ -299,8 +318,14 @@ class StackRun:
         try:
             for step in range(self.decode):
                 g = torch.cuda.CUDAGraph()
+                buf = step & 1
                 with torch.cuda.graph(g, stream=self.stream):
-                    self.session.enqueue(1, self._dec_tables[step & 1])
+                    self.session.enqueue(1, self._dec_tables[buf])
+                    if self.gathering:
+                        self.step_done.record(self.stream)
+                        self.comm.wait_event(self.step_done)
+                        self._gather(self.dec_gathered, self.dec_out[buf])
+                        self.stream.wait_stream(self.comm)
                 graphs.append(g)
         finally:
             self.session.set_layer_events(self.events)
@@ -365,13 +390,13 @@ def stack_costs(kinds, batch, prefill, decode, shape):
 
 
 def run_stack(torch, dist, world, rank, batch=16, prefill=8192, decode=256, layers=32,
-              shape=None, repeats=1, seed=SEED, graphs=True):
+              shape=None, repeats=1, seed=SEED, graphs=True, split="heads"):
     """Times `repeats` (prefill, decode) runs; returns rank-0 metrics (max over ranks).
     With `graphs` the decode steps are replayed from CUDA graphs captured
-    before the timed runs."""
+    before the timed runs.  `split` picks the ShardPlan."""
     shape = dict(QWEN35_4B if shape is None else shape)
     kinds = qwen35_kinds(layers)
-    plan = ShardPlan.make(world, rank, batch, shape)
+    plan = ShardPlan.make(world, rank, batch, shape, split)
     run = StackRun(torch, kinds, batch, prefill, decode, shape, plan, dist=dist, seed=seed)
     try:
         run.warmup()
@@ -412,10 +437,13 @@ def run_stack(torch, dist, world, rank, batch=16, prefill=8192, decode=256, laye
         "workload": (f"C5 hybrid stack: {kinds.count(LAYER_DELTANET)} DeltaNet + "
                      f"{kinds.count(LAYER_GQA)} GQA layers, batch {batch}, prefill {prefill}, "
                      f"{decode} decode steps"),
-        "sharding": {"sequence_groups": plan.seq_groups, "head_groups": plan.head_groups,
+        "sharding": {"split": split, "sequence_groups": plan.seq_groups,
+                     "head_groups": plan.head_groups,
                      "collective": "NCCL all-gather of head outputs (prefill: per layer, "
-                                   "overlapped; decode: all layers of a step in one)"
-                     if world > 1 else "none (1 GPU)"},
+                                   "overlapped; decode: all layers of a step in one, inside "
+                                   "the step's CUDA graph)"
+                     if world > 1 and plan.head_groups > 1 else
+                     "none (whole sequences per GPU)" if world > 1 else "none (1 GPU)"},
         "prefill_ms": round(p, 3),
         "prefill_tok_s": round(batch * prefill / (p / 1e3), 1),
         "prefill_tflops": round(2 * costs["prefill_macs"] / (p / 1e3) / 1e12, 2),
@@ -425,7 +453,8 @@ def run_stack(torch, dist, world, rank, batch=16, prefill=8192, decode=256, laye
         # Host time to issue the decode steps (rank 0): near decode_ms means launch-bound.
         "decode_host_issue_ms": round(statistics.median(issue_ms), 3),
         "repeats": repeats,
-        "decode_steps_from": "CUDA graphs captured per step" if graphs else "session enqueue",
+        "decode_steps_from": ("CUDA graphs captured per step (launches and collective)"
+                              if graphs else "session enqueue"),
         "cost_model": {"prefill_gflop": round(2 * costs["prefill_macs"] / 1e9, 1),
                        "prefill_gqa_gflop": round(2 * costs["prefill_gqa_macs"] / 1e9, 1),
                        "decode_gb": round(costs["decode_bytes"] / 1e9, 2)},
@@ -439,6 +468,7 @@ def main():
     p.add_argument("--decode-tokens", type=int, default=256)
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--repeats", type=int, default=1)
+    p.add_argument("--split", choices=["heads", "sequences"], default="heads")
     args = p.parse_args()
     import datetime
 
@@ -454,7 +484,7 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         r = run_stack(torch, dist, world, rank, args.batch, args.prefill_tokens,
-                      args.decode_tokens, args.layers, repeats=args.repeats)
+                      args.decode_tokens, args.layers, repeats=args.repeats, split=args.split)
         if rank == 0:
             # llmi-benchmark's report lines (tools/benchmark/Main.cpp:50-56).
             for phase, tokens, ms in (("Prefill", args.prefill_tokens, r["prefill_ms"]),

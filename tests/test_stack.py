@@ -45,7 +45,23 @@ def test_shard_plan_qwen35(world, seq_groups, head_groups):
         assert vh.start // 2 == kh.start and (vh.stop - 1) // 2 == kh.stop - 1
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sequence_major_plan(world):
+    plans = [S.ShardPlan.make(world, r, 16, S.QWEN35_4B, "sequences") for r in range(world)]
+    assert {(p.seq_groups, p.head_groups) for p in plans} == {(world, 1)}
+    owned = [b for p in plans for b in range(16)[p.seqs(16)]]
+    assert sorted(owned) == list(range(16))
+    assert all(p.heads(32) == slice(0, 32) for p in plans)
+    full = torch.randn(16, 3, 8, 4)
+    gathered = torch.stack([full[p.seqs(16)].reshape(16 // world, 3, -1) for p in plans])
+    assert torch.equal(S.unshard(gathered, world, world, 1), full.reshape(16, 3, -1))
+
+
 def test_shard_plan_rejects_impossible_split():
+    with pytest.raises(ValueError):
+        S.ShardPlan.make(3, 0, 16, S.QWEN35_4B, "sequences")
+    with pytest.raises(ValueError):
+        S.ShardPlan.make(2, 0, 16, S.QWEN35_4B, "rows")
     with pytest.raises(ValueError):
         S.ShardPlan.make(3, 0, 16, S.QWEN35_4B)
     with pytest.raises(ValueError):

@@ -20,8 +20,8 @@ KINDS = S.qwen35_kinds(4)  # three DeltaNet layers, then GQA
 BATCH, PREFILL, DECODE = 4, 80, 3
 
 
-def run_shard(world, rank):
-    plan = S.ShardPlan.make(world, rank, BATCH, SHAPE)
+def run_shard(world, rank, split="heads"):
+    plan = S.ShardPlan.make(world, rank, BATCH, SHAPE, split)
     run = S.StackRun(torch, KINDS, BATCH, PREFILL, DECODE, SHAPE, plan, dist=None, seed=11)
     try:
         run.run_prefill()
@@ -61,10 +61,11 @@ def test_stack_layers_match_oracle():
     check(host(pre[3]), want.reshape(BATCH, PREFILL, -1))
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_sharded_stack_reassembles_to_unsharded(world):
+@pytest.mark.parametrize("world,split", [(2, "heads"), (4, "heads"), (2, "sequences"),
+                                         (4, "sequences")])
+def test_sharded_stack_reassembles_to_unsharded(world, split):
     _, pre1, dec1, _ = run_shard(1, 0)
-    shards = [run_shard(world, r) for r in range(world)]
+    shards = [run_shard(world, r, split) for r in range(world)]
     plan = shards[0][0]
     for layer in range(len(KINDS)):
         gathered = torch.stack([s[1][layer] for s in shards])
