@@ -14,21 +14,26 @@ Keys of the line beyond the base contract:
                 CUDA events on its stream, against the measured HBM copy
                 bandwidth of MEASURED_PEAKS.json
   cpu_baseline  the reference's scalar check code restated in oracle/ (dense
-                fp64 causal GQA), built -O3 -march=native on this host and run
-                with every core on a bounded sample of the same workload
+                fp64 causal GQA, cacheAppend), built -O3 -march=native on this
+                host: the whole C2 step on every core, and 2 sequences on one
+                thread (one_thread_value); every secondary C1-C4 line carries
+                the same pair for its op
   e2e           the same step through the C-ABI calls with pinned host
                 buffers: H2D of q and the new rows, D2H of the output, timed;
                 the copies run on their own streams, double-buffered, under
                 the neighbouring steps' kernels
-  secondary     the other kernels of the path on their benchmark configs
-                (C1 prefill, C4 DeltaNet step, C3 DeltaNet prefill) and the
-                producers of its operands at the C5 layer shapes, each
-                run whole on every GPU (aggregate over N GPUs, max-over-ranks
-                time)
+  secondary     the other kernels of the path: C1 prefill (replicas), the
+                prefill at the C5 layer shape and the producers of its operands
+                (each whole on every GPU); C2, C3 and C4 as fixed jobs split
+                over the N GPUs (strong scaling: 64 sequences, 128 (sequence,
+                value head) units, 256 sequences), each with its time on one
+                GPU and the efficiency against it
   stack         the C5 hybrid stack (llminfer_b200/stack.py): 24 DeltaNet +
                 8 GQA layers, batch 16, prefill 8192 then 256 decode steps,
                 split by (sequence x head) over the N GPUs with an NCCL
                 all-gather of head outputs (strong scaling)
+  stack_sequence_major  (N > 1) the same stack with whole sequences per GPU,
+                which needs no collective
 `--impl reference` runs the reference arm: the CPU restatement of the
 reference's code (oracle/, "port") on the host cores, same metric.
 """
@@ -82,14 +87,17 @@ def load_peaks():
     return dict(FALLBACK_PEAKS, source="fallback")
 
 
-def profile_traffic(name: str):
-    """DRAM bytes per launch recorded in profiles/<name>.md ('traffic_bytes_per_launch: N')."""
-    import re
-    path = ROOT / "profiles" / f"{name}.md"
+def profile_traffic(name: str, op: str):
+    """DRAM bytes per call of `op` from profiles/traffic_<name>.jsonl, the output of
+    `kernel_bench traffic` over an ncu capture of the same workload (or None)."""
+    path = ROOT / "profiles" / f"traffic_{name}.jsonl"
     if not path.exists():
         return None
-    match = re.search(r"traffic_bytes_per_launch:\s*(\d+)", path.read_text())
-    return int(match.group(1)) if match else None
+    for text in path.read_text().splitlines():
+        line = json.loads(text)
+        if line.get("op") == op:
+            return line["measured_dram_bytes_per_call"]
+    return None
 
 
 class ClockSampler:
@@ -382,6 +390,7 @@ def run_ours(args, dist):
     peaks = load_peaks()
     P = C2["past"]
     q, kn, vn, kc, vc = decode_inputs(torch, device, SEED + dist.rank)
+    kc_bytes = kc.numel() * kc.element_size()
     out = torch.empty_like(q)
     ws = torch.empty(ops.decode_workspace_bytes(C2["batch"], C2["query_heads"], C2["kv_heads"],
                                                 C2["head_dim"], P), dtype=torch.uint8,
@@ -436,7 +445,7 @@ def run_ours(args, dist):
     ms_step = ms / K
     value = bytes_step * dist.world * K / (ms / 1e3) / 1e9
     achieved = bytes_decode / (decode_ms / 1e3) / 1e9
-    traffic = profile_traffic("gqa_decode_c2")
+    traffic = profile_traffic("c2_decode", "CausalGqa")
 
     # End to end through the C-ABI calls with pinned host buffers, pipelined
     # as a serving loop would run it: step i's inputs go up on one copy stream
@@ -547,7 +556,9 @@ def run_ours(args, dist):
             "query_heads": C2["query_heads"], "kv_heads": C2["kv_heads"],
             "head_dim": C2["head_dim"],
             "parallelism": f"sequence-sharded over {dist.world} GPU(s), no collective",
-            "l2": "no flush: each step streams 2.15 GB of KV cache, far above the 126 MB L2",
+            "l2": (f"no flush: each step streams {bytes_step / 1e9:.2f} GB of KV cache rows "
+                   f"(the caches hold {2 * kc_bytes / 1e9:.2f} GB at capacity), far above the "
+                   f"126 MB L2"),
             "bytes_per_step_per_gpu": bytes_step,
         },
         "roofline": {"kernel": "gqaScores+gqaSoftmax (decode op)", "bound": "hbm",

@@ -14,6 +14,8 @@ on the CPU before timing).  Prints one JSON object.
   python -m llminfer_b200.kernel_bench append  --batch 64 --tokens 1 --past 4096
   python -m llminfer_b200.kernel_bench rope    --batch 16 --tokens 8192 --past 0
   python -m llminfer_b200.kernel_bench deltaprep --batch 16 --tokens 8192
+  python -m llminfer_b200.kernel_bench traffic --csv launches.csv --workload decode \
+      --batch 64 --past 4096 --capacity 8192 [--out profiles/traffic_c2_decode.jsonl]
 """
 from __future__ import annotations
 
@@ -258,9 +260,108 @@ def bench_deltaprep(args):
                 peaks=src, check=check)
 
 
+# ---- measured DRAM traffic against the cost model (llmi graph --json counterpart) ----
+
+# Kernel-name fragments of this library's launches -> (GraphIR op, --plan name).
+KERNEL_DISPATCH = [
+    ("cache_append", "KvAppend", "cacheAppend"),
+    ("decode::partial", "CausalGqa", "gqaScores"),
+    ("decode::merge", "CausalGqa", "gqaSoftmax"),
+    ("gqa_prefill", "CausalGqa", "gqaFlashAttention"),
+    ("solve_pass", "DeltaUpdate", "graphDeltaUpdate"),
+    ("chunked_tc", "DeltaUpdate", "graphDeltaUpdate"),
+    ("recurrent", "DeltaUpdate", "graphDeltaUpdate"),
+]
+# The launch that starts one call of each op (a call may launch several kernels).
+CALL_MARKERS = {"KvAppend": "cache_append", "CausalGqa": ("decode::partial", "gqa_prefill"),
+                "DeltaUpdate": ("chunked_tc", "recurrent")}
+
+
+def read_ncu_csv(path):
+    """Launches of an `ncu --csv` metrics file: [(id, kernel name, {metric: value})]."""
+    import csv
+    lines = [l for l in Path(path).read_text().splitlines() if l.startswith('"')]
+    launches = {}
+    for row in csv.DictReader(lines):
+        key = row["ID"]
+        name = row["Kernel Name"]
+        value = float(row["Metric Value"].replace(",", ""))
+        unit = row.get("Metric Unit", "")
+        scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "nsecond": 1,
+                 "usecond": 1e3, "msecond": 1e6}.get(unit, 1)
+        launches.setdefault(key, (name, {}))[1][row["Metric Name"]] = value * scale
+    return [(k, n, m) for k, (n, m) in launches.items()]
+
+
+def traffic(args):
+    """Per GraphIR op of one call: the DRAM bytes ncu measured for this library's
+    kernels next to the cost model's logical bytes (llmi_cuda_describe_step, the
+    reference's Cost.cpp:85-93), from an ncu CSV of gpu__time_duration.sum,
+    dram__bytes_read.sum and dram__bytes_write.sum captured by hand."""
+    from . import describe_step, make_stack_config
+    launches = read_ncu_csv(args.csv)
+    per_op = {}
+    for _, name, metrics in launches:
+        hit = next(((op, plan) for frag, op, plan in KERNEL_DISPATCH if frag in name), None)
+        if hit is None:
+            continue
+        op, plan = hit
+        entry = per_op.setdefault(op, {"calls": 0, "dispatches": {}})
+        markers = CALL_MARKERS[op]
+        markers = (markers,) if isinstance(markers, str) else markers
+        if any(m in name for m in markers):
+            entry["calls"] += 1
+        d = entry["dispatches"].setdefault(plan, {"launches": 0, "time_ns": 0.0,
+                                                  "dram_bytes": 0.0, "kernels": []})
+        d["launches"] += 1
+        d["time_ns"] += metrics.get("gpu__time_duration.sum", 0.0)
+        d["dram_bytes"] += (metrics.get("dram__bytes_read.sum", 0.0)
+                            + metrics.get("dram__bytes_write.sum", 0.0))
+        short = name.split("(")[0]
+        if short not in d["kernels"]:
+            d["kernels"].append(short)
+    # Logical bytes of one call of each op at the workload's shape.
+    if args.workload == "delta":
+        Hk, Hv = args.delta_heads
+        dk, dv = args.delta_dims
+        cfg, keep = make_stack_config([0], 1, args.tokens, key_heads=Hk, key_dim=dk,
+                                      value_heads=Hv, value_dim=dv)
+        step = json.loads(describe_step(cfg, args.tokens, 0))
+    else:
+        T = 1 if args.workload == "decode" else args.tokens
+        cap = max(args.capacity, args.past + T)
+        cfg, keep = make_stack_config([1], 1, cap, query_heads=args.heads[0],
+                                      kv_heads=args.heads[1], head_dim=args.dim)
+        step = json.loads(describe_step(cfg, T, args.past))
+    logical = {op["kind"]: (op["cost"]["logical_read_bytes"] + op["cost"]["logical_write_bytes"])
+               * args.batch for op in step["ops"]}
+    lines = []
+    for op, entry in per_op.items():
+        calls = max(entry["calls"], 1)
+        measured = sum(d["dram_bytes"] for d in entry["dispatches"].values()) / calls
+        line = {"op": op, "workload": args.workload, "batch": args.batch, "calls": calls,
+                "dispatches": {k: {"launches": v["launches"],
+                                   "time_us_per_call": round(v["time_ns"] / calls / 1e3, 2),
+                                   "dram_bytes_per_call": int(v["dram_bytes"] / calls),
+                                   "kernels": v["kernels"]}
+                               for k, v in entry["dispatches"].items()},
+                "measured_dram_bytes_per_call": int(measured),
+                "logical_bytes_per_call": logical.get(op),
+                "measured_over_logical": (round(measured / logical[op], 4)
+                                          if logical.get(op) else None)}
+        lines.append(line)
+    return lines
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("op", choices=["decode", "prefill", "delta", "append", "rope", "deltaprep"])
+    p.add_argument("op", choices=["decode", "prefill", "delta", "append", "rope", "deltaprep",
+                                  "traffic"])
+    p.add_argument("--csv", help="traffic: ncu --csv file of gpu__time_duration.sum, "
+                                 "dram__bytes_read.sum, dram__bytes_write.sum")
+    p.add_argument("--workload", choices=["decode", "prefill", "delta"], default="decode",
+                   help="traffic: the shape the CSV was captured at (same flags as the op)")
+    p.add_argument("--out", help="traffic: also write the JSON lines to this file")
     p.add_argument("--batch", type=int, default=64)
     p.add_argument("--tokens", type=int, default=128)
     p.add_argument("--past", type=int, default=4096)
@@ -277,6 +378,13 @@ def main(argv=None):
     p.add_argument("--no-scratch", action="store_true",
                    help="delta: the entry point without scratch (llmi_cuda_delta_update)")
     args = p.parse_args(argv)
+    if args.op == "traffic":  # host only: no GPU needed
+        lines = traffic(args)
+        text = "\n".join(json.dumps(l) for l in lines) + "\n"
+        if args.out:
+            Path(args.out).write_text(text)
+        print(text, end="")
+        return
     torch.cuda.set_device(0)
     if args.op == "decode":
         res = bench_gqa(args, decode=True)
