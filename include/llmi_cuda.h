@@ -153,8 +153,8 @@ int llmi_cuda_delta_update(const llmi_delta_params *p, unsigned batch,
                            uint16_t *out, void *stream);
 
 /* Bytes of device scratch llmi_cuda_delta_update_ws needs for this shape: 8 KB
- * per (sequence, value head, 64-token chunk) when the call takes the
- * chunked tensor-core form, else 0.  Same graphDeltaUpdate dispatch
+ * per (sequence, value head, 64-token chunk) plus 16 KB per (sequence, key
+ * head, chunk) when the call takes the chunked tensor-core form, else 0.  Same graphDeltaUpdate dispatch
  * (MetalExecutionPlan.cpp:663-676); the scratch is this backend's own. */
 size_t llmi_cuda_delta_update_workspace(const llmi_delta_params *p, unsigned batch);
 

@@ -17,7 +17,12 @@
 // [64 t][64 s] fp16 in the 128-byte-swizzled K-major layout the second
 // pass's tcgen05 MMAs read (row t at t * 128 bytes, 16-byte chunk c of a row
 // at position c ^ (t & 7)), so the image is copied verbatim into shared
-// memory.  Requires key_dim == 128.
+// memory.  The pass also writes, per (sequence, key head, chunk), the k rows
+// it converted to fp16 as a 16 KB image in the second pass's [K; Q] operand
+// layout (two 8 KB blocks of 64 keys, the same swizzle), which replaces the
+// second pass's own fp32 staging and conversion at no extra HBM traffic (it
+// reads 16 KB of fp16 there instead of 32 KB of fp32).  Requires
+// key_dim == 128.
 //
 // Warp MMAs (m16n8k16, fp16 in, fp32 accumulation) do k k^T and the blocked
 // substitution; the 16x16 diagonal blocks are inverted by forward
@@ -37,7 +42,8 @@ constexpr int kThreads = 128;
 constexpr int kLdK = DK + 8;  // fp16 row stride of the k tile (conflict-free ldmatrix)
 constexpr int kLdA = 72;      // fp16 row stride of A
 constexpr int kLdT = 24;      // fp16 row stride of the diagonal-block inverses
-constexpr uint32_t kImageBytes = C * C * 2;  // one Tu image
+constexpr uint32_t kImageBytes = C * C * 2;     // one Tu image
+constexpr uint32_t kKImageBytes = C * DK * 2;   // one chunk's k rows
 
 struct Smem {
   __half k[C * kLdK];       // k rows of the chunk, fp16
@@ -56,9 +62,10 @@ __device__ __forceinline__ void frag_a(uint32_t (&f)[4], const __half *base, int
 }
 
 // Grid (chunks, key heads, batch), kThreads threads, sizeof(Smem) bytes of
-// dynamic shared memory.  tu: [batch][value heads][chunks] images.
+// dynamic shared memory.  tu_out: [batch][value heads][chunks] Tu images;
+// k_out: [batch][key heads][chunks] k-row images.
 __global__ void __launch_bounds__(kThreads)
-    solve_pass(const delta::Args a, uint8_t *__restrict__ tu_out) {
+    solve_pass(const delta::Args a, uint8_t *__restrict__ tu_out, uint8_t *__restrict__ k_out) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -87,6 +94,17 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   __syncthreads();
+  // The k rows' image for the second pass: 16-byte chunk ch of row t to
+  // block ch / 8, swizzled position (ch % 8) ^ (t % 8).
+  {
+    uint8_t *dst = k_out + ((size_t(seq) * a.key_heads + kh) * n_chunks + chunk) * kKImageBytes;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + kThreads * i, t = idx >> 4, ch = idx & 15;
+      *reinterpret_cast<uint4 *>(dst + (ch >> 3) * (kKImageBytes / 2) + sw128_chunk(t, ch & 7)) =
+          *reinterpret_cast<const uint4 *>(sm.k + t * kLdK + 8 * ch);
+    }
+  }
 
   // k k^T on the blocks at or below the diagonal: warp w owns rows
   // 16w..16w+15 and the column tiles 0..2w+1.

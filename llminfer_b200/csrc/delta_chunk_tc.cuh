@@ -60,6 +60,8 @@
 
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "delta_recurrent.cuh"
 #include "tcgen05.cuh"
@@ -112,21 +114,48 @@ struct Smem {
   static constexpr int graw = Tu + 8192;           // fp32 decay[64], beta[64] (cp.async)
   static constexpr int gates = graw + 2 * C * 4;   // Gates[kGateSets], by chunk mod kGateSets
   static constexpr int bars = gates + kGateSets * int(sizeof(Gates));
-  static constexpr int kBars = 16;
-  // Presolved form: Am, Ad and Td are unused; their 16 KB hold the y tile
-  // the IO group stores (the fused form stores it from Vp).
-  static constexpr int YsP = Am;
+  static constexpr int kBars = 19;
   static constexpr int tmem_slot = bars + kBars * 8;
   static constexpr int abort_flag = tmem_slot + 4;
   static constexpr int total = abort_flag + 12;
+  static constexpr int YsP = 0;  // presolved form only
 };
 static_assert(Smem::Tw % 1024 == 0 && Smem::P % 1024 == 0, "operand tiles 1024-byte aligned");
-static_assert(Smem::Tw - Smem::Am == 64 * 128 * 2, "the presolved y tile fits Am, Ad and Td");
 static_assert(sizeof(Gates) % 16 == 0, "gate sets stay 16-byte aligned");
 static_assert(Smem::total + 1024 <= 232448, "shared memory");
 
 constexpr uint32_t kVBytes = C * DV * 2, kKBytes = C * DK * 4;
-constexpr uint32_t kTuBytes = C * C * 2;  // one presolved Tu image
+constexpr uint32_t kTuBytes = C * C * 2;      // one presolved Tu image
+constexpr uint32_t kKImageBytes = C * DK * 2;  // one chunk's k rows, fp16, as the [K; Q] tile holds them
+
+// Shared memory of the presolved form.  The k rows arrive in fp16 in the
+// operand layout (bulk copies of the first pass's images), so there is no
+// fp32 staging tile and no A / solve scratch; that room holds a third
+// [K; Q] buffer (the IO group fills chunk n + 3 while chunks n .. n + 2 are
+// in flight) and the y tile the IO group stores.
+struct SmemP {
+  static constexpr int X = 0;                      // 3 x [K; Q] (32 KB each)
+  static constexpr int Vraw = X + 3 * 32768;
+  static constexpr int WB = Vraw + 16384;
+  static constexpr int Vp = WB + 16384;
+  static constexpr int Vg = Vp + 16384;
+  static constexpr int P = Vg + 16384;             // 3 x fp16 [64 t][64 s], one per [K; Q] buffer
+  static constexpr int YsP = P + 3 * 8192;         // y fp16 [64 t][128 dv] for the TMA store
+  static constexpr int Tw = YsP + 16384;
+  static constexpr int Tu = Tw + 8192;
+  static constexpr int graw = Tu + 8192;
+  static constexpr int gates = graw + 2 * C * 4;
+  static constexpr int bars = gates + kGateSets * int(sizeof(Gates));
+  static constexpr int kBars = Smem::kBars;
+  static constexpr int tmem_slot = bars + kBars * 8;
+  static constexpr int abort_flag = tmem_slot + 4;
+  static constexpr int total = abort_flag + 12;
+  // Fused-form members the shared code names but this form never reaches.
+  static constexpr int Kst = 0, Ys = 0, Am = 0, Ad = 0, Td = 0;
+};
+static_assert(SmemP::Tw % 1024 == 0 && SmemP::P % 1024 == 0 && SmemP::YsP % 1024 == 0 &&
+                  SmemP::Vraw % 1024 == 0, "operand tiles 1024-byte aligned");
+static_assert(SmemP::total + 1024 <= 232448, "shared memory (presolved)");
 
 // A tile 16x16 of a row-major fp16 [m][k] array (ldmatrix, mma.m16n8k16 layout).
 __device__ __forceinline__ void load_a(uint32_t (&f)[4], const __half *base, int ld, int m0, int k0,
@@ -175,14 +204,19 @@ __device__ __forceinline__ void load32(float (&d)[32], const float *p) {
 // Presolved: the chunk-local systems were solved beforehand for every chunk
 // at once (delta_chunk_solve.cuh); `solved` holds one 8 KB image of
 // Tu = T diag(beta) per (sequence, value head, chunk), which arrives with the
-// chunk's v boxes.  The local chain then skips A and the solve: warps 0-1
-// scale Tu's columns by e^{G_s} into Tw while warps 2-3 make P.
+// chunk's v boxes, and `kimages` one 16 KB image of the chunk's k rows in
+// fp16 per (sequence, key head, chunk), copied straight into the [K; Q]
+// buffer.  The local chain then skips A and the solve: warps 0-1 scale Tu's
+// columns by e^{G_s} into Tw while warps 2-3 make P.  Grid as above,
+// kThreadsPresolved threads, SmemP::total + 1024 bytes.
 template <bool Presolved>
 __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
     chunked_tc(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                const __grid_constant__ CUtensorMap map_v,
                const __grid_constant__ CUtensorMap map_out, const delta::Args a,
-               const uint8_t *__restrict__ solved) {
+               const uint8_t *__restrict__ solved, const uint8_t *__restrict__ kimages) {
+  using Smem = std::conditional_t<Presolved, SmemP, delta_tc::Smem>;
+  constexpr uint32_t kXBufs = Presolved ? 3 : 2;  // [K; Q] (and P) buffers
   extern __shared__ uint8_t smem_raw[];
   // Rounded up to 1024 bytes by an offset from the shared array itself, so
   // the compiler keeps every access through `smem` a shared-memory one (a
@@ -203,13 +237,21 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
   uint64_t *bar_m4 = bars + 5;      // M4 done (state)
   uint64_t *bar_wb = bars + 6;      // M4 done: W tile free (state -> local)
   uint64_t *bar_m56 = bars + 7;     // M5/M6 done (state)
-  uint64_t *bar_xready = bars + 8;  // [2] [K; Q] and P buffers released by M5/M6 and the q
-                                    //     rows of the buffer's next chunk written (state -> local)
-  uint64_t *bar_du = bars + 10;     // U read from TMEM (state -> local)
-  uint64_t *bar_k = bars + 11;      // k rows staged (state)
-  uint64_t *bar_gates = bars + 12;  // [2] gates of the chunks of each parity (state or IO -> local)
-  uint64_t *bar_m6 = bars + 14;     // presolved: M6 done (state)
-  uint64_t *bar_yread = bars + 15;  // presolved: chunk's QS and Dy read from TMEM (IO -> state)
+  uint64_t *bar_xready = bars + 8;  // [kXBufs] [K; Q] and P buffers released by M5/M6 and the
+                                    //     k and q rows of the buffer's next chunk written
+                                    //     (state or IO -> local)
+  uint64_t *bar_du = bars + 11;     // U read from TMEM (state -> local)
+  uint64_t *bar_k = bars + 12;      // k rows staged (state or IO)
+  uint64_t *bar_gates = bars + 13;  // [2 fused, 4 presolved] gates of a chunk (state or IO -> local)
+  uint64_t *bar_m6 = bars + 17;     // presolved: M6 done (state)
+  uint64_t *bar_yread = bars + 18;  // presolved: chunk's QS and Dy read from TMEM (IO -> state)
+  // Chunk c's [K; Q] buffer, and its gates' barrier and parity: the presolved
+  // form runs the groups up to three chunks apart, so its gates barriers are
+  // four deep (no barrier can then be two phases ahead of a waiter).
+  auto xbuf = [](uint32_t c) { return Presolved ? c % 3 : c & 1; };
+  auto xready_parity = [](uint32_t c) { return Presolved ? (c / 3) & 1 : (c >> 1) & 1; };
+  auto gate_bar = [&](uint32_t c) { return &bar_gates[Presolved ? c & 3 : c & 1]; };
+  auto gate_parity = [](uint32_t c) { return Presolved ? (c >> 2) & 1 : (c >> 1) & 1; };
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Smem::tmem_slot);
   volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(smem + Smem::abort_flag);
   float *graw = reinterpret_cast<float *>(smem + Smem::graw);
@@ -297,13 +339,24 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
     __syncwarp();
   };
   auto issue_k = [&](uint32_t chunk) {
-    mbar_arrive_expect_tx(bar_k, kKBytes);
-    tma_load_3d(smem + Smem::Kst, &map_k, int(kh * DK), int(chunk * C), int(seq), bar_k);
+    if constexpr (Presolved) {
+      // The chunk's k rows in fp16, straight into its [K; Q] buffer (both
+      // 64-key blocks); read by both value heads of the key head.
+      mbar_arrive_expect_tx(bar_k, kKImageBytes);
+      const uint8_t *src =
+          kimages + ((size_t(seq) * a.key_heads + kh) * n_chunks + chunk) * kKImageBytes;
+      uint8_t *xb = smem + Smem::X + xbuf(chunk) * 32768;
+      bulk_g2s(xb, src, kKImageBytes / 2, bar_k, policy_evict_last());
+      bulk_g2s(xb + 16384, src + kKImageBytes / 2, kKImageBytes / 2, bar_k, policy_evict_last());
+    } else {
+      mbar_arrive_expect_tx(bar_k, kKBytes);
+      tma_load_3d(smem + Smem::Kst, &map_k, int(kh * DK), int(chunk * C), int(seq), bar_k);
+    }
   };
   // Staged k rows of `chunk` (fp32) into rows 0-63 of its [K; Q] buffer
   // (fp16); every thread must have seen bar_k complete.
   auto convert_k = [&](uint32_t chunk) {
-    uint8_t *Xb = smem + Smem::X + (chunk & 1) * 32768;
+    uint8_t *Xb = smem + Smem::X + xbuf(chunk) * 32768;
     const float *kr = reinterpret_cast<const float *>(smem + Smem::Kst);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -333,7 +386,7 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
     }
   };
   auto store_q = [&](uint32_t chunk, const float4 (&qr)[8][2]) {
-    uint8_t *Xb = smem + Smem::X + (chunk & 1) * 32768;
+    uint8_t *Xb = smem + Smem::X + xbuf(chunk) * 32768;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int idx = gt + kGroup * i, t = idx >> 4, ch = idx & 15;
@@ -364,13 +417,14 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
 
     for (uint32_t n = 0; n < n_chunks; ++n) {
       const int b = n & 1;
+      const uint32_t xb = xbuf(n);
       Gates &gs = gate_sets[n % kGateSets];
-      const uint32_t xs = sbase + Smem::X + b * 32768;
+      const uint32_t xs = sbase + Smem::X + xb * 32768;
       const bool more = n + 1 < n_chunks;
 
       // L1. [K; Q] buffer b holds chunk n's k and q rows (fp16, written by
       //     the state group once M5/M6 of chunk n - 2 released it).
-      bool fail = !wait_or_abort(&bar_xready[b], (n >> 1) & 1, abort);
+      bool fail = !wait_or_abort(&bar_xready[xb], xready_parity(n), abort);
       if (named_sync_or(kBarLocal, kGroup, fail))
         break;
 
@@ -387,7 +441,7 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
         m1_pending = int(n & 1);
       }
       fail = !wait_or_abort(bar_m1, n & 1, abort) ||
-             !wait_or_abort(&bar_gates[n & 1], (n >> 1) & 1, abort);
+             !wait_or_abort(gate_bar(n), gate_parity(n), abort);
       if (named_sync_or(kBarLocal, kGroup, fail))
         break;
       m1_pending = -1;
@@ -404,7 +458,7 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
       {
         __half *Am = reinterpret_cast<__half *>(smem + Smem::Am);
         float *Ad = reinterpret_cast<float *>(smem + Smem::Ad);
-        uint8_t *Pb = smem + Smem::P + b * 8192;
+        uint8_t *Pb = smem + Smem::P + xb * 8192;
         const bool arow = warp < 2;
         const int hr = warp & 1;
         const int t = 32 * hr + lane;
@@ -947,7 +1001,7 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
     // Initial state: S^T into TMEM in fp16 (M4's A operand) and in fp32 (the
     // accumulator M6 adds to), the latter scaled by chunk 0's e^{G_C}, which
     // the IO group derives first.
-    bool fail = elected && !wait_or_abort(&bar_gates[0], 0, abort);
+    bool fail = elected && !wait_or_abort(gate_bar(0), gate_parity(0), abort);
     const bool pro_fail = named_sync_or(kBarState, kGroup, fail);
     if (!pro_fail) {
       const float egl0 = gate_sets[0].egl[0];
@@ -977,7 +1031,7 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
       const int b = n & 1;
       const bool last = n + 1 == n_chunks;
       const Gates &gs = gate_sets[n % kGateSets];
-      const uint32_t xs = sbase + Smem::X + b * 32768;
+      const uint32_t xs = sbase + Smem::X + xbuf(n) * 32768;
 
       // P1. Chunk n's W, [K; Q], P and U are ready: M4's W half (S^T W^T),
       //     which V' needs, then its Q half (S^T Q^T) once the IO group has
@@ -1051,7 +1105,7 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
 #pragma unroll
         for (int k = 0; k < C / 16; ++k)
           mma_ss(tmem + kColY, desc_add(smem_desc(sbase + Smem::Vp, 16, 1024), k * 32),
-                 desc_add(smem_desc(sbase + Smem::P + b * 8192, 16, 1024), k * 32), id5,
+                 desc_add(smem_desc(sbase + Smem::P + xbuf(n) * 8192, 16, 1024), k * 32), id5,
                  k > 0 ? 1u : 0u);
         mma_commit(bar_m56);
         m6_pending = m56_pending = int(n & 1);
@@ -1060,7 +1114,7 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
       //     fp32 accumulator scaled by the next chunk's e^{G_C} for its M6 (or,
       //     after the last chunk, the state to memory).
       fail = !wait_or_abort(bar_m6, n & 1, abort) ||
-             (!last && !wait_or_abort(&bar_gates[(n + 1) & 1], ((n + 1) >> 1) & 1, abort));
+             (!last && !wait_or_abort(gate_bar(n + 1), gate_parity(n + 1), abort));
       if (named_sync_or(kBarState, kGroup, fail))
         break;
       m6_pending = -1;
@@ -1101,29 +1155,30 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
     }
   } else {
     // ================== IO group, presolved form (warps 8-11) ==================
-    // The chunk's gates, its k and q rows into [K; Q] two chunks ahead, and
-    // y = e^G (Q S) + P V' from TMEM to memory one chunk behind.
+    // The chunks' gates two ahead of the local chain; chunk n + 3's k rows
+    // (bulk copy of their fp16 image) and q rows (converted) into the [K; Q]
+    // buffer chunk n's MMAs release; y = e^G (Q S) + P V' from TMEM to
+    // memory one chunk behind the state chain.
     const bool elected = gt == 0;
     const int dv = gt;
     int k_pending = -1;
-    if (elected) {
-      issue_k(0);
-      k_pending = 0;
-      if (n_chunks > 2)
-        tma_prefetch_3d(&map_q, int(kh * DK), 2 * C, int(seq));
-    }
     if (warp == 8) {
       for (uint32_t c = 0; c < 2 && c < n_chunks; ++c) {
         issue_gates(c);
         gates(c);
         if (lane == 0)
-          mbar_arrive(&bar_gates[c]);
+          mbar_arrive(gate_bar(c));
       }
       if (n_chunks > 2)
         issue_gates(2);
     }
+    // [K; Q] buffers of chunks 0-2.
     bool pro_fail = false;
-    for (uint32_t c = 0; c < 2 && c < n_chunks; ++c) {
+    for (uint32_t c = 0; c < kXBufs && c < n_chunks; ++c) {
+      if (elected) {
+        issue_k(c);
+        k_pending = int(c & 1);
+      }
       float4 qr[8][2];
       load_q(c, qr);
       bool f = false;
@@ -1136,38 +1191,39 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
         pro_fail = true;
         break;
       }
-      convert_k(c);
       store_q(c, qr);
       named_sync(kBarIO, kGroup);
-      if (elected && c + 1 < n_chunks) {
-        issue_k(c + 1);
-        k_pending = int((c + 1) & 1);
-      }
-    }
-    if (elected && !pro_fail) {
-      mbar_arrive(&bar_xready[0]);
-      if (n_chunks > 1)
-        mbar_arrive(&bar_xready[1]);
+      if (elected)
+        mbar_arrive(&bar_xready[xbuf(c)]);
     }
     for (uint32_t n = 0; n < n_chunks && !pro_fail; ++n) {
-      const int b = n & 1;
       const uint32_t t0 = n * C;
       const Gates &gs = gate_sets[n % kGateSets];
-      // Q1. Chunk n's M4 (Q half), M5 and M6 are done; the previous output
-      //     tile has left shared memory.
+      // Q1. Gates of chunk n + 2 (they need only the decay and beta rows).
+      if (warp == 8 && n + 2 < n_chunks) {
+        gates(n + 2);
+        if (n + 3 < n_chunks)
+          issue_gates(n + 3);
+        if (lane == 0)
+          mbar_arrive(gate_bar(n + 2));
+      }
+      // Q2. Chunk n's M4 (Q half), M5 and M6 are done, which releases its
+      //     [K; Q] buffer: chunk n + 3's k rows start to arrive in it.  The
+      //     previous output tile has left shared memory.
       if (elected)
         bulk_wait_read();
       bool fail = !wait_or_abort(bar_m56, n & 1, abort);
       if (named_sync_or(kBarIO, kGroup, fail))
         break;
       tc_fence_after();
-      float4 qr[8][2];
-      const bool q_next = n + 2 < n_chunks;
-      if (q_next)
-        load_q(n + 2, qr);
-      if (elected && n + 3 < n_chunks)
-        tma_prefetch_3d(&map_q, int(kh * DK), int(t0 + 3 * C), int(seq));
-      // Q2. y^T = e^G (Q S)^T + Dy into the output tile, then to memory.
+      const bool refill = n + kXBufs < n_chunks;
+      if (elected && refill) {
+        issue_k(n + kXBufs);
+        k_pending = int((n + kXBufs) & 1);
+        if (n + kXBufs + 1 < n_chunks)
+          tma_prefetch_3d(&map_q, int(kh * DK), int(t0 + (kXBufs + 1) * C), int(seq));
+      }
+      // Q3. y^T = e^G (Q S)^T + Dy into the output tile, then to memory.
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         uint32_t ya[32], yd[32];
@@ -1190,36 +1246,22 @@ __global__ void __launch_bounds__(Presolved ? kThreadsPresolved : kThreads, 1)
         tma_store_3d(&map_out, smem + Smem::YsP, int(vh * DV), int(t0), int(seq));
         bulk_commit();
       }
-      // Q3. [K; Q] buffer b is free: chunk n + 2's k and q rows into it;
-      //     the staging tile then takes chunk n + 3's k rows.
-      if (q_next) {
+      // Q4. Chunk n + 3's q rows into the buffer; then it is ready.
+      if (refill) {
+        float4 qr[8][2];
+        load_q(n + kXBufs, qr);
         fail = false;
         if (elected) {
-          fail = !wait_or_abort(bar_k, n & 1, abort);
+          fail = !wait_or_abort(bar_k, (n + kXBufs) & 1, abort);
           if (!fail)
             k_pending = -1;
         }
         if (named_sync_or(kBarIO, kGroup, fail))
           break;
-        convert_k(n + 2);
-        store_q(n + 2, qr);
+        store_q(n + kXBufs, qr);
         named_sync(kBarIO, kGroup);
-        if (elected) {
-          if (n + 3 < n_chunks) {
-            issue_k(n + 3);
-            k_pending = int((n + 3) & 1);
-          }
-          mbar_arrive(&bar_xready[b]);
-        }
-      }
-      // Q4. Gates of chunk n + 2, which the local chain reads at its step L3
-      //     and the state chain at the end of chunk n + 1.
-      if (warp == 8 && n + 2 < n_chunks) {
-        gates(n + 2);
-        if (n + 3 < n_chunks)
-          issue_gates(n + 3);
-        if (lane == 0)
-          mbar_arrive(&bar_gates[n & 1]);
+        if (elected)
+          mbar_arrive(&bar_xready[xbuf(n)]);
       }
     }
     if (elected) {

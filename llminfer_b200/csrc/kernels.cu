@@ -750,9 +750,18 @@ bool delta_chunked(const llmi_delta_params *p, unsigned batch, const void *q, co
          batch <= 65535 && p->valueHeads <= 2147483647u && p->keyHeads <= 65535;
 }
 
-size_t delta_solved_bytes(const llmi_delta_params *p, unsigned batch) {
+// Scratch of the chunk-parallel form: the Tu images of every (sequence,
+// value head, chunk), then the fp16 k-row images of every (sequence, key
+// head, chunk).
+size_t delta_tu_bytes(const llmi_delta_params *p, unsigned batch) {
   const uint64_t chunks = (uint64_t(p->tokens) + delta_tc::C - 1) / delta_tc::C;
   return size_t(uint64_t(batch) * p->valueHeads * chunks * delta_tc::kTuBytes);
+}
+
+size_t delta_solved_bytes(const llmi_delta_params *p, unsigned batch) {
+  const uint64_t chunks = (uint64_t(p->tokens) + delta_tc::C - 1) / delta_tc::C;
+  return delta_tu_bytes(p, batch) +
+         size_t(uint64_t(batch) * p->keyHeads * chunks * delta_tc::kKImageBytes);
 }
 
 int delta_update_impl(const llmi_delta_params *p, unsigned batch, const float *q, const float *k,
@@ -864,6 +873,7 @@ int delta_update_impl(const llmi_delta_params *p, unsigned batch, const float *q
         return e;
     }
     const size_t smem = delta_tc::Smem::total + 1024;
+    const size_t smem_p = delta_tc::SmemP::total + 1024;
     dim3 grid(p->valueHeads, batch);
     if (presolve) {
       // Every chunk's triangular system at once, then the state recurrence.
@@ -871,21 +881,24 @@ int delta_update_impl(const llmi_delta_params *p, unsigned batch, const float *q
       if (int e = allow_smem(reinterpret_cast<const void *>(delta_solve::solve_pass), solve_smem,
                              dev))
         return e;
-      if (int e = allow_smem(reinterpret_cast<const void *>(delta_tc::chunked_tc<true>), smem, dev))
+      if (int e = allow_smem(reinterpret_cast<const void *>(delta_tc::chunked_tc<true>), smem_p,
+                             dev))
         return e;
       const uint32_t chunks = (p->tokens + delta_tc::C - 1) / delta_tc::C;
       uint8_t *solved = static_cast<uint8_t *>(workspace);
+      uint8_t *kimages = solved + delta_tu_bytes(p, batch);
       delta_solve::solve_pass<<<dim3(chunks, p->keyHeads, batch), delta_solve::kThreads,
-                                solve_smem, s>>>(a, solved);
+                                solve_smem, s>>>(a, solved, kimages);
       if (int e = launched("graphDeltaUpdate (chunk systems)"))
         return e;
-      delta_tc::chunked_tc<true><<<grid, delta_tc::kThreadsPresolved, smem, s>>>(mq, mk, mv, mo, a,
-                                                                                solved);
+      delta_tc::chunked_tc<true><<<grid, delta_tc::kThreadsPresolved, smem_p, s>>>(
+          mq, mk, mv, mo, a, solved, kimages);
       return launched("graphDeltaUpdate (chunked, presolved, tcgen05)");
     }
     if (int e = allow_smem(reinterpret_cast<const void *>(delta_tc::chunked_tc<false>), smem, dev))
       return e;
-    delta_tc::chunked_tc<false><<<grid, delta_tc::kThreads, smem, s>>>(mq, mk, mv, mo, a, nullptr);
+    delta_tc::chunked_tc<false><<<grid, delta_tc::kThreads, smem, s>>>(mq, mk, mv, mo, a, nullptr,
+                                                                      nullptr);
     return launched("graphDeltaUpdate (chunked, tcgen05)");
   }
   const bool fast = p->valueDim == 128 && (p->keyDim == 128 || p->keyDim == 64) &&
