@@ -42,6 +42,7 @@ constexpr int kThreads = 128;
 constexpr int kLdK = DK + 8;  // fp16 row stride of the k tile (conflict-free ldmatrix)
 constexpr int kLdA = 72;      // fp16 row stride of A
 constexpr int kLdT = 24;      // fp16 row stride of the diagonal-block inverses
+constexpr int kMaxGroup = 4;                    // value heads per key head held at once
 constexpr uint32_t kImageBytes = C * C * 2;     // one Tu image
 constexpr uint32_t kKImageBytes = C * DK * 2;   // one chunk's k rows
 
@@ -50,8 +51,8 @@ struct Smem {
   __half am[C * kLdA];      // A, fp16 (blocks below the diagonal are read)
   float ad[4 * 16 * 16];    // diagonal blocks of A, fp32, [block][s][t]
   __half td[C * kLdT];      // inverses of the diagonal blocks of I + A, fp16
-  float g2[C];              // G_t in log2 units
-  float bet[C];             // beta_t (0 past the last token)
+  float g2[kMaxGroup][C];   // per value head of the key head: G_t in log2 units
+  float bet[kMaxGroup][C];  // beta_t (0 past the last token)
   alignas(128) uint8_t tu[kImageBytes];  // the Tu image
 };
 
@@ -64,7 +65,7 @@ __device__ __forceinline__ void frag_a(uint32_t (&f)[4], const __half *base, int
 // Grid (chunks, key heads, batch), kThreads threads, sizeof(Smem) bytes of
 // dynamic shared memory.  tu_out: [batch][value heads][chunks] Tu images;
 // k_out: [batch][key heads][chunks] k-row images.
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 5)
     solve_pass(const delta::Args a, uint8_t *__restrict__ tu_out, uint8_t *__restrict__ k_out) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
@@ -74,23 +75,56 @@ __global__ void __launch_bounds__(kThreads)
   const uint32_t t0 = chunk * C;
   const int valid = int(min(uint32_t(C), a.tokens - t0));
 
-  // k rows of the chunk (fp32, 512 B each) into the fp16 tile; rows past the
-  // last token are zero.
+  // Gates of value head vh into slot j: G (log2 units, inclusive cumulative
+  // sum of log2 decay; pad tokens decay 1, beta 0).  A decay of exactly 0
+  // gets log2 -1e4, so every factor across it is 0.  One warp.
+  auto gates = [&](uint32_t vh, int j) {
+    const size_t tok0 = size_t(seq) * a.tokens + t0;
+    float la[2], bb[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int t = 2 * lane + i;
+      const bool in = t < valid;
+      const float d = in ? a.decay[(tok0 + t) * a.value_heads + vh] : 1.f;
+      la[i] = in ? (d > 0.f ? fast_log2(d) : -1e4f) : 0.f;
+      bb[i] = in ? a.beta[(tok0 + t) * a.value_heads + vh] : 0.f;
+    }
+    const float pair = la[0] + la[1];
+    float incl = pair;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off)
+        incl += y;
+    }
+    sm.g2[j][2 * lane] = incl - pair + la[0];
+    sm.g2[j][2 * lane + 1] = incl;
+    sm.bet[j][2 * lane] = bb[0];
+    sm.bet[j][2 * lane + 1] = bb[1];
+  };
+  // k rows of the chunk (fp32, 512 B each) into the fp16 tile, in two
+  // rounds of loads; rows past the last token are zero.  The gates of up to
+  // kMaxGroup value heads are derived while the first round is in flight.
   {
     const float *src = a.k + (size_t(seq) * a.tokens + t0) * a.key_heads * DK + size_t(kh) * DK;
     const size_t row_stride = size_t(a.key_heads) * DK;
-    float4 r[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int idx = tid + kThreads * i, t = idx >> 5, c4 = idx & 31;
-      r[i] = t < valid ? ld_stream_f4(src + size_t(t) * row_stride + 4 * c4)
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    for (int round = 0; round < 2; ++round) {
+      float4 r[8];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int idx = tid + kThreads * i, t = idx >> 5, c4 = idx & 31;
-      *reinterpret_cast<uint2 *>(sm.k + t * kLdK + 4 * c4) =
-          make_uint2(pack_half2(r[i].x, r[i].y), pack_half2(r[i].z, r[i].w));
+      for (int i = 0; i < 8; ++i) {
+        const int idx = tid + kThreads * (8 * round + i), t = idx >> 5, c4 = idx & 31;
+        r[i] = t < valid ? ld_stream_f4(src + size_t(t) * row_stride + 4 * c4)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      if (round == 0 && a.group <= uint32_t(kMaxGroup) && warp < int(a.group))
+        gates(kh * a.group + warp, warp);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int idx = tid + kThreads * (8 * round + i), t = idx >> 5, c4 = idx & 31;
+        *reinterpret_cast<uint2 *>(sm.k + t * kLdK + 4 * c4) =
+            make_uint2(pack_half2(r[i].x, r[i].y), pack_half2(r[i].z, r[i].w));
+      }
     }
   }
   __syncthreads();
@@ -134,52 +168,32 @@ __global__ void __launch_bounds__(kThreads)
   }
 
   const int g = lane >> 2;
+  const bool gates_ahead = a.group <= uint32_t(kMaxGroup);
   for (uint32_t vh = kh * a.group; vh < (kh + 1) * a.group; ++vh) {
-    // Gates of this value head: G (log2 units, inclusive cumulative sum of
-    // log2 decay; pad tokens decay 1, beta 0).  A decay of exactly 0 gets
-    // log2 -1e4, so every factor across it is 0.
-    if (warp == 0) {
-      const size_t tok0 = size_t(seq) * a.tokens + t0;
-      float la[2], bb[2];
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int t = 2 * lane + i;
-        const bool in = t < valid;
-        const float d = in ? a.decay[(tok0 + t) * a.value_heads + vh] : 1.f;
-        la[i] = in ? (d > 0.f ? fast_log2(d) : -1e4f) : 0.f;
-        bb[i] = in ? a.beta[(tok0 + t) * a.value_heads + vh] : 0.f;
-      }
-      const float pair = la[0] + la[1];
-      float incl = pair;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off)
-          incl += y;
-      }
-      sm.g2[2 * lane] = incl - pair + la[0];
-      sm.g2[2 * lane + 1] = incl;
-      sm.bet[2 * lane] = bb[0];
-      sm.bet[2 * lane + 1] = bb[1];
+    const int j = gates_ahead ? int(vh - kh * a.group) : 0;
+    if (!gates_ahead) {
+      if (warp == 0)
+        gates(vh, 0);
+      __syncthreads();
     }
-    __syncthreads();
+    const float *g2 = sm.g2[j], *bet = sm.bet[j];
 
     // A from the dot products: beta_t (k_t . k_s) 2^(G_t - G_s) for s < t.
     // fp16 rows into am, the diagonal blocks also in fp32 (column-major).
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int t = 16 * warp + g + 8 * half;
-      const float g_t = sm.g2[t], b_t = sm.bet[t];
+      const float g_t = g2[t], b_t = bet[t];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (j < 2 * warp + 2) {
-          const int s = 8 * j + 2 * (lane & 3);
+      for (int jt = 0; jt < 8; ++jt) {
+        if (jt < 2 * warp + 2) {
+          const int s = 8 * jt + 2 * (lane & 3);
           float v[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e)
-            v[e] = s + e < t ? b_t * dots[j][2 * half + e] * fast_exp2(g_t - sm.g2[s + e]) : 0.f;
+            v[e] = s + e < t ? b_t * dots[jt][2 * half + e] * fast_exp2(g_t - g2[s + e]) : 0.f;
           *reinterpret_cast<uint32_t *>(sm.am + t * kLdA + s) = pack_half2(v[0], v[1]);
-          if (j >= 2 * warp) {  // the diagonal block
+          if (jt >= 2 * warp) {  // the diagonal block
 #pragma unroll
             for (int e = 0; e < 2; ++e)
               sm.ad[warp * 256 + ((s + e) & 15) * 16 + (t & 15)] = v[e];
@@ -226,7 +240,7 @@ __global__ void __launch_bounds__(kThreads)
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int e = 0; e < 2; ++e)
-          su[nt][e] = sm.bet[16 * warp + 8 * nt + 2 * (lane & 3) + e];
+          su[nt][e] = bet[16 * warp + 8 * nt + 2 * (lane & 3) + e];
       uint32_t xb[4][2][2];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {

@@ -72,10 +72,11 @@ def test_delta_prefill_config_reduced(form):
     check(case, *run(case, form))
 
 
-@pytest.mark.parametrize("hk,hv", [(4, 4), (2, 8), (1, 3)])
+@pytest.mark.parametrize("hk,hv", [(4, 4), (2, 8), (1, 3), (1, 6)])
 def test_presolved_groups(hk, hv):
-    # Key heads shared by 1, 4 and 3 value heads: the solve pass walks the
-    # value heads of its key head; ragged last chunk, a decay of exactly 0.
+    # Key heads shared by 1, 4, 3 and 6 value heads: the solve pass walks the
+    # value heads of its key head (up to 4 with their gates derived up front,
+    # more one at a time); ragged last chunk, a decay of exactly 0.
     case = _inputs.delta_case(2, 150, hk, 128, hv, 128, state_std=0.02, seed=hv)
     case["decay"][1, 70, 0] = 0.0
     check(case, *run(case, "presolved"))
