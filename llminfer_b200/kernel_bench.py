@@ -312,14 +312,18 @@ def traffic(args):
         if any(m in name for m in markers):
             entry["calls"] += 1
         d = entry["dispatches"].setdefault(plan, {"launches": 0, "time_ns": 0.0,
-                                                  "dram_bytes": 0.0, "kernels": []})
+                                                  "dram_bytes": 0.0, "kernels": {}})
+        t_ns = metrics.get("gpu__time_duration.sum", 0.0)
+        nbytes = (metrics.get("dram__bytes_read.sum", 0.0)
+                  + metrics.get("dram__bytes_write.sum", 0.0))
         d["launches"] += 1
-        d["time_ns"] += metrics.get("gpu__time_duration.sum", 0.0)
-        d["dram_bytes"] += (metrics.get("dram__bytes_read.sum", 0.0)
-                            + metrics.get("dram__bytes_write.sum", 0.0))
-        short = name.split("(")[0]
-        if short not in d["kernels"]:
-            d["kernels"].append(short)
+        d["time_ns"] += t_ns
+        d["dram_bytes"] += nbytes
+        kern = d["kernels"].setdefault(name.split("(")[0].replace("void ", ""),
+                                       {"launches": 0, "time_ns": 0.0, "dram_bytes": 0.0})
+        kern["launches"] += 1
+        kern["time_ns"] += t_ns
+        kern["dram_bytes"] += nbytes
     # Logical bytes of one call of each op at the workload's shape.
     if args.workload == "delta":
         Hk, Hv = args.delta_heads
@@ -343,7 +347,12 @@ def traffic(args):
                 "dispatches": {k: {"launches": v["launches"],
                                    "time_us_per_call": round(v["time_ns"] / calls / 1e3, 2),
                                    "dram_bytes_per_call": int(v["dram_bytes"] / calls),
-                                   "kernels": v["kernels"]}
+                                   "kernels": {n: {"launches": kv["launches"],
+                                                   "time_us_per_call":
+                                                       round(kv["time_ns"] / calls / 1e3, 2),
+                                                   "dram_bytes_per_call":
+                                                       int(kv["dram_bytes"] / calls)}
+                                               for n, kv in v["kernels"].items()}}
                                for k, v in entry["dispatches"].items()},
                 "measured_dram_bytes_per_call": int(measured),
                 "logical_bytes_per_call": logical.get(op),
