@@ -675,12 +675,16 @@ __global__ void __launch_bounds__(128) partial_simt(const Args a) {
 }
 
 // ---------------------------------------------------------------------------
-// Merge pass: one CTA per (sequence, kv head), one warp per query head.  Lane
-// i reads record i's max and sum once (records past 32 fold in with a loop),
-// the shuffled maximum gives every record's weight, and lane i's weight is
-// broadcast by shuffle where the outputs are summed.  The outputs are summed
-// with float4 loads, four records per round, so a unit's records cost a few
-// dependent load rounds rather than one per record.  Launched as a
+// Merge pass: one CTA per (sequence, kv head) and slice of head_dim, one warp
+// per query head.  Lane i reads record i's max and sum once (records past 32
+// fold in with a loop), the shuffled maximum gives every record's weight,
+// and lane i's weight is broadcast by shuffle where the outputs are summed.
+// head_dim is cut into gridDim.y slices so that few (sequence, kv head)
+// units with many records (a GPU's shard of a few sequences or kv heads)
+// still spread over many SMs.  Within a slice of F float4 columns, lanes
+// form 32 / F groups that sum interleaved records (F < 32), or each lane
+// owns F / 32 columns (F >= 32); loads go four records per round, and the
+// groups' sums are combined by shuffles at the end.  Launched as a
 // programmatic dependent of the partial pass: it may start while that grid
 // drains and waits for it here.
 constexpr int kMergeThreads = 128;
@@ -696,6 +700,8 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   const bool grouped = pt.heads > 1;
   const uint32_t unit = grouped ? seq : out_unit, head = grouped ? kvh : 0u;
   const uint32_t G = a.group, D = a.head_dim;
+  // This CTA's columns [d0, d1) of head_dim.
+  const uint32_t slice = D / gridDim.y, d0 = blockIdx.y * slice, d1 = d0 + slice;
   const uint32_t w_lo = uint32_t((uint64_t(unit) * pt.tiles_per_unit) / pt.tiles_per_worker);
   const uint32_t w_hi =
       uint32_t((uint64_t(unit + 1) * pt.tiles_per_unit - 1) / pt.tiles_per_worker);
@@ -705,9 +711,9 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
     return a.records + record_index(pt, w_lo + i, unit, head) * a.record_floats;
   };
   // float4 path: every head's output row starts on a 16-byte boundary
-  // (records are, and 2G and D are multiples of 4) and the fp16 output rows
-  // on an 8-byte one.
-  const bool vec = ((2 * G) & 3u) == 0 && (D & 3u) == 0 &&
+  // (records are, and 2G and D are multiples of 4), the slice is whole
+  // float4 columns and the fp16 output rows start on an 8-byte boundary.
+  const bool vec = ((2 * G) & 3u) == 0 && (D & 3u) == 0 && (slice & 3u) == 0 &&
                    (reinterpret_cast<uintptr_t>(a.out) & 7u) == 0;
   wait_primary();
   __half *out = a.out + (size_t(seq) * a.kv_heads * G + kvh * G) * D;
@@ -733,31 +739,34 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1)
       sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    // Record i's weight (i is uniform over the warp).
+    // Record i's weight; every lane of the warp calls this (it shuffles).
     auto weight = [&](uint32_t i) {
       const float w = __shfl_sync(0xffffffffu, w_own, int(i & 31u));
-      return i < 32 ? w : fast_exp2(record(i)[h] - top);
+      return i < 32 ? w : (i < n ? fast_exp2(record(i)[h] - top) : 0.f);
     };
     const float inv = 1.f / sum;
     if (vec) {
-      // Lane l owns the float4 chunks l, l + 32, ... of the row (D <= 512).
+      const uint32_t F = (d1 - d0) / 4;                 // float4 columns in the slice
+      const uint32_t R = F < 32 ? 32 / F : 1;           // record groups of lanes
+      const uint32_t g = F < 32 ? lane / F : 0, f = F < 32 ? lane % F : lane;
+      const uint32_t c0 = d0 / 4;
       float4 acc[kMergeMaxPerLane / 4];
 #pragma unroll
       for (int k = 0; k < kMergeMaxPerLane / 4; ++k)
         acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (uint32_t i0 = 0; i0 < n; i0 += kMergeRound) {
+      for (uint32_t i0 = 0; i0 < n; i0 += R * kMergeRound) {
         float4 v[kMergeRound][kMergeMaxPerLane / 4];
         float w[kMergeRound];
 #pragma unroll
         for (int j = 0; j < kMergeRound; ++j) {
-          const uint32_t i = i0 + j;
-          w[j] = i < n ? weight(i) : 0.f;
+          const uint32_t i = i0 + g + R * j;
+          w[j] = weight(i);
           const float4 *o =
               reinterpret_cast<const float4 *>(record(min(i, n - 1)) + 2 * G + h * D);
 #pragma unroll
           for (int k = 0; k < kMergeMaxPerLane / 4; ++k) {
-            const uint32_t c = lane + 32 * k;
-            v[j][k] = (i < n && 4 * c < D) ? o[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+            const uint32_t c = f + 32 * k;
+            v[j][k] = (i < n && c < F) ? o[c0 + c] : make_float4(0.f, 0.f, 0.f, 0.f);
           }
         }
 #pragma unroll
@@ -770,13 +779,22 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
             acc[k].w = fmaf(v[j][k].w, w[j], acc[k].w);
           }
       }
+      // Sum the record groups (lanes f, f + F, f + 2F, ...).
+      for (uint32_t off = F; off < 32 && F < 32; off <<= 1) {
+        acc[0].x += __shfl_xor_sync(0xffffffffu, acc[0].x, int(off));
+        acc[0].y += __shfl_xor_sync(0xffffffffu, acc[0].y, int(off));
+        acc[0].z += __shfl_xor_sync(0xffffffffu, acc[0].z, int(off));
+        acc[0].w += __shfl_xor_sync(0xffffffffu, acc[0].w, int(off));
+      }
+      if (g == 0) {
 #pragma unroll
-      for (int k = 0; k < kMergeMaxPerLane / 4; ++k) {
-        const uint32_t c = lane + 32 * k;
-        if (4 * c < D)
-          *reinterpret_cast<uint2 *>(out + h * D + 4 * c) =
-              make_uint2(pack_half2(acc[k].x * inv, acc[k].y * inv),
-                         pack_half2(acc[k].z * inv, acc[k].w * inv));
+        for (int k = 0; k < kMergeMaxPerLane / 4; ++k) {
+          const uint32_t c = f + 32 * k;
+          if (c < F)
+            *reinterpret_cast<uint2 *>(out + h * D + 4 * (c0 + c)) =
+                make_uint2(pack_half2(acc[k].x * inv, acc[k].y * inv),
+                           pack_half2(acc[k].z * inv, acc[k].w * inv));
+        }
       }
     } else {
       float acc[kMergeMaxPerLane];
@@ -789,15 +807,15 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
         const float *o = record(i) + 2 * G + h * D;
 #pragma unroll
         for (int k = 0; k < kMergeMaxPerLane; ++k) {
-          const uint32_t d = lane + 32 * k;
-          if (d < D)
+          const uint32_t d = d0 + lane + 32 * k;
+          if (d < d1)
             acc[k] = fmaf(o[d], w, acc[k]);
         }
       }
 #pragma unroll
       for (int k = 0; k < kMergeMaxPerLane; ++k) {
-        const uint32_t d = lane + 32 * k;
-        if (d < D)
+        const uint32_t d = d0 + lane + 32 * k;
+        if (d < d1)
           out[h * D + d] = __float2half_rn(acc[k] * inv);
       }
     }

@@ -666,7 +666,14 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
     return status;
   // The merge may be scheduled while the partial grid drains; it waits for
   // it on the device.
-  return launch_dependent("gqaSoftmax (decode merge)", decode::merge, dim3(batch * p->kvHeads),
+  // head_dim slices per (sequence, kv head): enough merge CTAs for about two
+  // per SM, each slice at least 32 columns and a whole number of float4s.
+  const uint32_t units = batch * p->kvHeads;
+  uint32_t slices = 1;
+  while (uint64_t(units) * slices * 2 <= 2ull * uint64_t(dev.sm_count) && p->headDim % (slices * 8) == 0 &&
+         p->headDim / (slices * 2) >= 32)
+    slices *= 2;
+  return launch_dependent("gqaSoftmax (decode merge)", decode::merge, dim3(units, slices),
                           dim3(decode::kMergeThreads), 0, s, a);
 }
 

@@ -100,6 +100,7 @@ def test_prefill_matches_dense_oracle(batch, tokens, past, hq, hkv, d):
     (4, 8320, 16, 4, 256),     # C5 decode shape: over 32 partial records per sequence
     (3, 500, 8, 2, 128),       # CTA workers, head_dim 128
     (8, 2000, 4, 1, 256),      # CTA workers, one kv head (a head-sharded rank's shape)
+    (2, 8320, 16, 4, 256),     # a sequence-major 8-GPU rank: 74 records per unit, merge in 8 slices
     (2, 3000, 16, 1, 128),     # group of 16: CUDA-core path, keys in groups of four
 ])
 def test_decode_matches_oracles(batch, past, hq, hkv, d):
