@@ -801,6 +801,7 @@ def run_secondary(torch, ops, device, peaks, dist):
     # conv + SiLU + q/k L2 norm and gates.  Bytes: each operand read and
     # written once.
     B, T, D = 16, 8192, 256
+    Hk, dk, Hv, dv = 16, 128, 32, 128
     qg = torch.randn(B, T, 16, 2 * D, generator=g, device=device).half()
     kr = torch.randn(B, T, 4, D, generator=g, device=device).half()
     wq = (0.1 * torch.randn(D, generator=g, device=device)).float()
