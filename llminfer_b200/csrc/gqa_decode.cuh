@@ -746,9 +746,12 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
     };
     const float inv = 1.f / sum;
     if (vec) {
-      const uint32_t F = (d1 - d0) / 4;                 // float4 columns in the slice
-      const uint32_t R = F < 32 ? 32 / F : 1;           // record groups of lanes
-      const uint32_t g = F < 32 ? lane / F : 0, f = F < 32 ? lane % F : lane;
+      const uint32_t F = (d1 - d0) / 4;  // float4 columns in the slice
+      // Record groups of lanes when F is a power of two below 32 (the
+      // groups' sums then combine by xor shuffles); else one group.
+      const bool grouped_lanes = F < 32 && (F & (F - 1)) == 0;
+      const uint32_t R = grouped_lanes ? 32 / F : 1;
+      const uint32_t g = grouped_lanes ? lane / F : 0, f = grouped_lanes ? lane % F : lane;
       const uint32_t c0 = d0 / 4;
       float4 acc[kMergeMaxPerLane / 4];
 #pragma unroll
@@ -780,7 +783,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
           }
       }
       // Sum the record groups (lanes f, f + F, f + 2F, ...).
-      for (uint32_t off = F; off < 32 && F < 32; off <<= 1) {
+      for (uint32_t off = F; grouped_lanes && off < 32; off <<= 1) {
         acc[0].x += __shfl_xor_sync(0xffffffffu, acc[0].x, int(off));
         acc[0].y += __shfl_xor_sync(0xffffffffu, acc[0].y, int(off));
         acc[0].z += __shfl_xor_sync(0xffffffffu, acc[0].z, int(off));
