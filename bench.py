@@ -747,6 +747,31 @@ def run_strong(torch, ops, device, peaks, dist, g):
     return out
 
 
+def time_abi_calls(torch, ops, q, kc, vc, out, dist, reps=200):
+    """Per-call time of llmi_cuda_gqa_prefill called straight through ctypes with its
+    arguments prepared once, `reps` calls back to back between two events: the C
+    entry point's host cost (checks, cached tensor maps, launch) where it exceeds
+    the kernel's device time."""
+    import ctypes
+    abi = ops.abi
+    p = abi.GqaParams(q.shape[1], q.shape[2], kc.shape[2], q.shape[3], 0)
+    args = (ctypes.byref(p), q.shape[0], q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+            kc.stride(0), out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    call = abi.lib.llmi_cuda_gqa_prefill
+    for _ in range(10):
+        abi.check(call(*args))
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        call(*args)
+    b.record()
+    torch.cuda.synchronize()
+    return dist.max(a.elapsed_time(b) / reps)
+
+
 def run_secondary(torch, ops, device, peaks, dist):
     """The other kernels of the path on their benchmark configs (CUDA events, median,
     max over ranks).  Every rank runs the whole config on its own GPU, so with N GPUs
@@ -762,6 +787,7 @@ def run_secondary(torch, ops, device, peaks, dist):
     out = torch.empty_like(q)
     med, best = time_op(torch, lambda: ops.gqa_prefill(q, kc, vc, 0, out=out), dist)
     graph_ms = time_graph(torch, lambda: ops.gqa_prefill(q, kc, vc, 0, out=out), dist)
+    abi_ms = time_abi_calls(torch, ops, q, kc, vc, out, dist)
     macs = step_bytes([1], 128, 0, 128, 1, query_heads=16, kv_heads=4, head_dim=256)["CausalGqa"][1]
     tf = 2 * macs / (med / 1e3) / 1e12
     tf_graph = 2 * macs / (graph_ms / 1e3) / 1e12
@@ -769,8 +795,10 @@ def run_secondary(torch, ops, device, peaks, dist):
                             + (f", {N} replicas" if N > 1 else ""),
                 "ms": round(med, 4), "value": round(tf * N, 3), "unit": "TFLOP/s",
                 "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4),
-                # Launch-bound: the same call captured in a CUDA graph and replayed.
-                "graph_replay_ms": round(graph_ms, 4), "graph_replay_value": round(tf_graph * N, 3)})
+                # Launch-bound: the same call captured in a CUDA graph and replayed,
+                # and the C-ABI call alone issued back to back (no Python wrapper).
+                "graph_replay_ms": round(graph_ms, 4), "graph_replay_value": round(tf_graph * N, 3),
+                "c_abi_call_ms": round(abi_ms, 4)})
     del q, kc, vc, out
     # The GQA prefill at one C5 layer's shape: B=16 (per GPU), T=8192, past 0.
     # Each launch is ~9 ms and the loop runs under the power cap, so the

@@ -63,7 +63,7 @@ def gqa_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, p
     p = _gqa_params(q, k_cache, past)
     out = torch.empty_like(q) if out is None else out
     _need(out, torch.float16, "out")
-    stride = k_cache[0].numel()
+    stride = k_cache.stride(0)
     check(lib.llmi_cuda_gqa_prefill(ctypes.byref(p), q.shape[0], q.data_ptr(),
                                     k_cache.data_ptr(), v_cache.data_ptr(), stride,
                                     out.data_ptr(), _stream(stream)))
@@ -91,7 +91,7 @@ def gqa_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pa
         workspace = torch.empty(n, dtype=torch.uint8, device=q.device)
     out = torch.empty_like(q) if out is None else out
     _need(out, torch.float16, "out")
-    stride = k_cache[0].numel()
+    stride = k_cache.stride(0)
     check(lib.llmi_cuda_gqa_decode(ctypes.byref(p), q.shape[0], q.data_ptr(),
                                    k_cache.data_ptr(), v_cache.data_ptr(), stride,
                                    out.data_ptr(), workspace.data_ptr(), workspace.numel(),

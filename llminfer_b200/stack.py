@@ -413,6 +413,12 @@ def run_stack(torch, dist, world, rank, batch=16, prefill=8192, decode=256, laye
             ev[0].record(run.stream)
             run.run_prefill()
             ev[1].record(run.stream)
+            # The decode steps are issued once the prefill has finished, so the
+            # host time below is the issue cost alone (not time spent blocked
+            # on a launch queue that the prefill keeps full).  The device
+            # interval starts at ev[1], so it includes any host lag.
+            run.join()
+            run.stream.synchronize()
             t0 = time.perf_counter()
             for s in range(decode):
                 run.run_decode_step(s)
@@ -450,7 +456,8 @@ def run_stack(torch, dist, world, rank, batch=16, prefill=8192, decode=256, laye
         "decode_ms": round(d, 3),
         "decode_tok_s": round(batch * decode / (d / 1e3), 1),
         "decode_gbs": round(costs["decode_bytes"] / (d / 1e3) / 1e9, 1),
-        # Host time to issue the decode steps (rank 0): near decode_ms means launch-bound.
+        # Host time to issue the decode steps after the prefill (rank 0): at or
+        # above decode_ms means the device waited for the host.
         "decode_host_issue_ms": round(statistics.median(issue_ms), 3),
         "repeats": repeats,
         "decode_steps_from": ("CUDA graphs captured per step (launches and collective)"
