@@ -55,6 +55,30 @@ def time_fn(fn, samples: int, warmup: int):
     return ms[0], statistics.median(ms)
 
 
+def time_graph(fn, reps: int = 50):
+    """Device time per call of fn captured once into a CUDA graph and replayed
+    `reps` times back to back between two events (no Python wrapper per call):
+    the measure for launch-bound shapes."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
 def torch_gqa(q, kc, vc, past, rows):
     """fp32 causal GQA for the listed (seq, token, head) rows."""
     B, T, Hq, D = q.shape
@@ -97,6 +121,7 @@ def bench_gqa(args, decode: bool):
         got = torch.stack([out[s, t, h].float() for s, t, h in rows])
         check = dict(zip(("max_abs", "rel_l2"), errors(got, want)))
     best, med = time_fn(fn, args.samples, args.warmup)
+    graph_ms = time_graph(fn) if args.graph else None
     rows_read = args.past + T
     nbytes = B * (2 * T * Hq * D * 2 + 2 * rows_read * Hkv * D * 2)
     pairs = T * args.past + T * (T + 1) // 2
@@ -107,6 +132,9 @@ def bench_gqa(args, decode: bool):
                gbs=nbytes / (med * 1e-3) / 1e9, tflops=flops / (med * 1e-3) / 1e12,
                hbm_frac=nbytes / (med * 1e-3) / 1e9 / hbm, tensor_frac=flops / (med * 1e-3) / 1e12 / tf,
                peaks=src, check=check)
+    if graph_ms is not None:
+        res.update(graph_ms=graph_ms, graph_gbs=nbytes / (graph_ms * 1e-3) / 1e9,
+                   graph_hbm_frac=nbytes / (graph_ms * 1e-3) / 1e9 / hbm)
     return res
 
 
@@ -384,6 +412,8 @@ def main(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--seed", type=int, default=179531)
     p.add_argument("--no-check", action="store_true")
+    p.add_argument("--graph", action="store_true",
+                   help="decode/prefill: also time the call replayed from a CUDA graph")
     p.add_argument("--no-scratch", action="store_true",
                    help="delta: the entry point without scratch (llmi_cuda_delta_update)")
     args = p.parse_args(argv)
