@@ -691,6 +691,7 @@ constexpr int kMergeThreads = 128;
 constexpr int kMergeMaxGroup = 64;
 constexpr int kMergeMaxPerLane = 16;  // head_dim <= 512
 constexpr int kMergeRound = 4;        // records per round of float4 loads
+constexpr int kMergeSmemRecords = 512;  // records per unit whose weights are staged in smem
 
 __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   launch_dependents();
@@ -715,32 +716,62 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   // float4 columns and the fp16 output rows start on an 8-byte boundary.
   const bool vec = ((2 * G) & 3u) == 0 && (D & 3u) == 0 && (slice & 3u) == 0 &&
                    (reinterpret_cast<uintptr_t>(a.out) & 7u) == 0;
+  // Up to kMergeSmemRecords records per unit: the warp stages every record's
+  // max and sum in shared memory with independent loads, then turns them into
+  // weights there, so the output sums below read weights from shared memory
+  // instead of chaining a global load per record.
+  __shared__ float staged[kMergeThreads / 32][2][kMergeSmemRecords];
+  const bool stage = n <= uint32_t(kMergeSmemRecords);
   wait_primary();
   __half *out = a.out + (size_t(seq) * a.kv_heads * G + kvh * G) * D;
   for (uint32_t h = warp; h < G; h += kMergeThreads / 32) {
-    float m_own = -INFINITY, l_own = 0.f;
-    if (uint32_t(lane) < n) {
-      const float *r = record(lane);
-      m_own = r[h];
-      l_own = r[G + h];
-    }
-    float top = m_own;
-    for (uint32_t i = lane + 32; i < n; i += 32)
-      top = fmaxf(top, record(i)[h]);
+    float *sm_w = staged[warp][0], *sm_l = staged[warp][1];
+    float top = -INFINITY, sum = 0.f, w_own = 0.f;
+    if (stage) {
+#pragma unroll 4
+      for (uint32_t i = lane; i < n; i += 32) {
+        const float *r = record(i);
+        const float m = r[h];
+        sm_w[i] = m;
+        sm_l[i] = r[G + h];
+        top = fmaxf(top, m);
+      }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-      top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, off));
-    const float w_own = uint32_t(lane) < n ? fast_exp2(m_own - top) : 0.f;
-    float sum = l_own * w_own;
-    for (uint32_t i = lane + 32; i < n; i += 32) {
-      const float *r = record(i);
-      sum = fmaf(r[G + h], fast_exp2(r[h] - top), sum);
+      for (int off = 16; off > 0; off >>= 1)
+        top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, off));
+      for (uint32_t i = lane; i < n; i += 32) {
+        const float w = fast_exp2(sm_w[i] - top);
+        sm_w[i] = w;
+        sum = fmaf(sm_l[i], w, sum);
+      }
+      __syncwarp();
+    } else {
+      float m_own = -INFINITY, l_own = 0.f;
+      if (uint32_t(lane) < n) {
+        const float *r = record(lane);
+        m_own = r[h];
+        l_own = r[G + h];
+      }
+      top = m_own;
+      for (uint32_t i = lane + 32; i < n; i += 32)
+        top = fmaxf(top, record(i)[h]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+        top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, off));
+      w_own = uint32_t(lane) < n ? fast_exp2(m_own - top) : 0.f;
+      sum = l_own * w_own;
+      for (uint32_t i = lane + 32; i < n; i += 32) {
+        const float *r = record(i);
+        sum = fmaf(r[G + h], fast_exp2(r[h] - top), sum);
+      }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1)
       sum += __shfl_xor_sync(0xffffffffu, sum, off);
     // Record i's weight; every lane of the warp calls this (it shuffles).
     auto weight = [&](uint32_t i) {
+      if (stage)
+        return i < n ? sm_w[i] : 0.f;
       const float w = __shfl_sync(0xffffffffu, w_own, int(i & 31u));
       return i < 32 ? w : (i < n ? fast_exp2(record(i)[h] - top) : 0.f);
     };
@@ -789,6 +820,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
         acc[0].z += __shfl_xor_sync(0xffffffffu, acc[0].z, int(off));
         acc[0].w += __shfl_xor_sync(0xffffffffu, acc[0].w, int(off));
       }
+      __syncwarp();  // the staged weights are rewritten for the warp's next head
       if (g == 0) {
 #pragma unroll
         for (int k = 0; k < kMergeMaxPerLane / 4; ++k) {
@@ -815,6 +847,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
             acc[k] = fmaf(o[d], w, acc[k]);
         }
       }
+      __syncwarp();  // the staged weights are rewritten for the warp's next head
 #pragma unroll
       for (int k = 0; k < kMergeMaxPerLane; ++k) {
         const uint32_t d = d0 + lane + 32 * k;

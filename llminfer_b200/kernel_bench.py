@@ -291,17 +291,18 @@ def bench_deltaprep(args):
 # ---- measured DRAM traffic against the cost model (llmi graph --json counterpart) ----
 
 # Kernel-name fragments of this library's launches -> (GraphIR op, --plan name).
+# (ncu shows the names with or without their namespaces.)
 KERNEL_DISPATCH = [
     ("cache_append", "KvAppend", "cacheAppend"),
-    ("decode::partial", "CausalGqa", "gqaScores"),
-    ("decode::merge", "CausalGqa", "gqaSoftmax"),
+    ("partial_", "CausalGqa", "gqaScores"),
+    ("merge(", "CausalGqa", "gqaSoftmax"),
     ("gqa_prefill", "CausalGqa", "gqaFlashAttention"),
     ("solve_pass", "DeltaUpdate", "graphDeltaUpdate"),
     ("chunked_tc", "DeltaUpdate", "graphDeltaUpdate"),
     ("recurrent", "DeltaUpdate", "graphDeltaUpdate"),
 ]
 # The launch that starts one call of each op (a call may launch several kernels).
-CALL_MARKERS = {"KvAppend": "cache_append", "CausalGqa": ("decode::partial", "gqa_prefill"),
+CALL_MARKERS = {"KvAppend": "cache_append", "CausalGqa": ("partial_", "gqa_prefill"),
                 "DeltaUpdate": ("chunked_tc", "recurrent")}
 
 
