@@ -655,34 +655,43 @@ def run_strong(torch, ops, device, peaks, dist, g):
         med, _ = time_op(torch, fn, dist, reps=reps, warmup=warmup)
         return med, nbytes
 
+    def whole_on_one_gpu(make, reps, warmup):
+        """Rank 0 times the whole job alone on its GPU before any shard runs
+        (the other ranks wait at the barrier); returns ms or None."""
+        if N == 1:
+            return None
+        dist.barrier()
+        one = None
+        if dist.rank == 0:
+            fn, _ = make(True)
+            for _ in range(warmup + 3):
+                fn()
+            torch.cuda.synchronize()
+            evs = [(torch.cuda.Event(enable_timing=True),
+                    torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+            for a, b in evs:
+                a.record()
+                fn()
+                b.record()
+            torch.cuda.synchronize()
+            one = statistics.median(a.elapsed_time(b) for a, b in evs)
+            del fn
+        torch.cuda.empty_cache()
+        dist.barrier()
+        return one
+
     def line(name, unit_desc, make, total_bytes, reps=10, warmup=3):
+        one = whole_on_one_gpu(make, reps, warmup)
         ms, _ = measure(make, reps, warmup, whole=False)
         gbs = total_bytes / (ms / 1e3) / 1e9
         entry = {"workload": name, "scaling": "strong", "split": unit_desc,
                  "ms": round(ms, 4), "value": round(gbs, 1), "unit": "GB/s",
                  "frac_of_hbm_peak_per_gpu": round(gbs / N / peaks["hbm_gbs"], 4)}
-        # The whole job on one GPU (rank 0; the other ranks wait at the barrier).
-        if N > 1:
-            dist.barrier()
-            if dist.rank == 0:
-                fn, _ = make(True)
-                for _ in range(warmup):
-                    fn()
-                torch.cuda.synchronize()
-                evs = [(torch.cuda.Event(enable_timing=True),
-                        torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-                for a, b in evs:
-                    a.record()
-                    fn()
-                    b.record()
-                torch.cuda.synchronize()
-                one = statistics.median(a.elapsed_time(b) for a, b in evs)
-                entry["ms_1gpu"] = round(one, 4)
-                entry["efficiency_vs_1gpu"] = round(one / (N * ms), 4)
-            dist.barrier()
-        else:
-            entry["ms_1gpu"] = round(ms, 4)
-            entry["efficiency_vs_1gpu"] = 1.0
+        if N == 1:
+            one = ms
+        if dist.rank == 0:
+            entry["ms_1gpu"] = round(one, 4)
+            entry["efficiency_vs_1gpu"] = round(one / (N * ms), 4)
         torch.cuda.empty_cache()
         return entry
 
