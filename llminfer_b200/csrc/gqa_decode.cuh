@@ -788,7 +788,29 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
 #pragma unroll
       for (int k = 0; k < kMergeMaxPerLane / 4; ++k)
         acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (uint32_t i0 = 0; i0 < n; i0 += R * kMergeRound) {
+      if (grouped_lanes) {
+        // One float4 column per lane: eight records' loads per round.
+        constexpr int kWide = 2 * kMergeRound;
+        for (uint32_t i0 = 0; i0 < n; i0 += R * kWide) {
+          float4 v[kWide];
+          float w[kWide];
+#pragma unroll
+          for (int j = 0; j < kWide; ++j) {
+            const uint32_t i = i0 + g + R * j;
+            w[j] = weight(i);
+            v[j] = i < n ? reinterpret_cast<const float4 *>(record(i) + 2 * G + h * D)[c0 + f]
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int j = 0; j < kWide; ++j) {
+            acc[0].x = fmaf(v[j].x, w[j], acc[0].x);
+            acc[0].y = fmaf(v[j].y, w[j], acc[0].y);
+            acc[0].z = fmaf(v[j].z, w[j], acc[0].z);
+            acc[0].w = fmaf(v[j].w, w[j], acc[0].w);
+          }
+        }
+      }
+      for (uint32_t i0 = 0; !grouped_lanes && i0 < n; i0 += R * kMergeRound) {
         float4 v[kMergeRound][kMergeMaxPerLane / 4];
         float w[kMergeRound];
 #pragma unroll

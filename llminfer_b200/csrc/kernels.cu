@@ -667,11 +667,11 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
   // The merge may be scheduled while the partial grid drains; it waits for
   // it on the device.
   // head_dim slices per (sequence, kv head): enough merge CTAs for about two
-  // per SM, each slice at least 32 columns and a whole number of float4s.
+  // per SM, each slice at least 16 columns and a whole number of float4s.
   const uint32_t units = batch * p->kvHeads;
   uint32_t slices = 1;
-  while (uint64_t(units) * slices * 2 <= 2ull * uint64_t(dev.sm_count) && p->headDim % (slices * 8) == 0 &&
-         p->headDim / (slices * 2) >= 32)
+  while (uint64_t(units) * slices * 2 <= 2ull * uint64_t(dev.sm_count) &&
+         p->headDim % (slices * 8) == 0 && p->headDim / (slices * 2) >= 16)
     slices *= 2;
   return launch_dependent("gqaSoftmax (decode merge)", decode::merge, dim3(units, slices),
                           dim3(decode::kMergeThreads), 0, s, a);
