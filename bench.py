@@ -878,7 +878,7 @@ def run_secondary(torch, ops, device, peaks, dist):
     # The GQA prefill at one C5 layer's shape: B=16 (per GPU), T=8192, past 0.
     # Measured last: at the power cap it leaves the next few milliseconds of
     # work on the GPU slower.
-    # Each launch is ~9 ms and the loop runs under the power cap, so the
+    # Each launch is ~6 ms and the loop runs under the power cap, so the
     # sustained peak is the denominator that applies; burst is given too.
     B, T = 16, 8192
     q = torch.randn(B, T, 16, 256, generator=g, device=device).half()
