@@ -108,6 +108,29 @@ int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch,
                          uint16_t *out, void *workspace,
                          size_t workspace_bytes, void *stream);
 
+/* KvAppend followed by CausalGqa with tokens == 1, in the decode's kernels: the
+ * cacheAppend pair of the step's KvAppend (Reference.metal:295-301, lowered
+ * at MetalExecutionPlan.cpp:516-522) and the decode above (:536-548), as the
+ * reference's graph orders them (Graph.cpp:263-267).  Same result as
+ *   llmi_cuda_cache_append(keys), llmi_cuda_cache_append(values),
+ *   llmi_cuda_gqa_decode
+ * with offset past*kvHeads*headDim and count kvHeads*headDim: after the call
+ * row `past` of each sequence's caches holds k_new / v_new and `out` is the
+ * decode over rows [0, past].  k_new, v_new: [batch][kvHeads][headDim] fp16
+ * at sequence stride new_stride; either may be null when that cache row is
+ * already written (e.g. keys written by llmi_cuda_norm_rope).  The partial
+ * pass reads row `past` from k_new / v_new and the merge pass writes it into
+ * the caches, which saves the two append launches of a decode step; shapes
+ * that take the CUDA-core pass, and new rows that are not 16-byte aligned,
+ * run the appends first as their own launches.  Workspace as
+ * llmi_cuda_gqa_decode. */
+int llmi_cuda_gqa_decode_append(const llmi_gqa_params *p, unsigned batch,
+                                const uint16_t *q, const uint16_t *k_new,
+                                const uint16_t *v_new, size_t new_stride,
+                                uint16_t *k_cache, uint16_t *v_cache,
+                                size_t cache_stride, uint16_t *out, void *workspace,
+                                size_t workspace_bytes, void *stream);
+
 /* Decode without a caller-provided workspace.  This entry point has no
  * counterpart in the reference.  It exists for callers that cannot allocate
  * device memory: an executor that hands out all device memory from its own

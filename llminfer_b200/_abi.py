@@ -113,6 +113,9 @@ SIGNATURES = [
     ("llmi_cuda_gqa_decode", c_int,
      [POINTER(GqaParams), c_uint, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p,
       c_void_p, c_size_t, c_void_p]),
+    ("llmi_cuda_gqa_decode_append", c_int,
+     [POINTER(GqaParams), c_uint, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p,
+      c_size_t, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("llmi_cuda_gqa_decode_noalloc", c_int,
      [POINTER(GqaParams), c_uint, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     ("llmi_cuda_delta_update", c_int,

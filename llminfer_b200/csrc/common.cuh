@@ -37,8 +37,9 @@ __device__ __forceinline__ void raise_error(unsigned bits) { atomicOr(&g_error_w
 // programmatic stream serialization may become resident once every CTA of the
 // kernel before it has called launch_dependents() (or exited); wait_primary()
 // then blocks until that kernel has completed and its memory is visible.
-// Decode-path kernels call both at entry, before any global access or early
-// return: the next launch's set-up and CTA ramp overlap this one's tail, and
+// Decode-path kernels call both at entry, before any global access (L2
+// prefetches aside) or early return: the next launch's set-up and CTA ramp
+// overlap this one's tail, and
 // since every kernel waits for its predecessor before finishing, the chain
 // stays ordered.  Without the launch attribute both are no-ops.
 __device__ __forceinline__ void launch_dependents() {
@@ -185,6 +186,14 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
       "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+}
+
+// Bulk prefetch of [src, src + bytes) into L2: no destination, no barrier.
+// src 16-byte aligned, bytes a multiple of 16.  A prefetch only warms L2 and
+// never changes what a later load returns, so a kernel may issue it before
+// wait_primary(), while the kernel ahead of it still runs.
+__device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {

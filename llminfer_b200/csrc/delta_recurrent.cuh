@@ -34,7 +34,6 @@ constexpr int kRecWarps = 8;
 // dv == 128, dk == DK (multiple of 8, <= 128).  Grid (Hv, batch), 256 threads.
 template <int DK>
 __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v128(const Args a) {
-  pdl_enter();
   constexpr int R = DK / kRecWarps;  // state rows per warp
   constexpr int DV = 128;
   __shared__ float4 red_pred[kRecWarps][32];
@@ -43,6 +42,11 @@ __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v128(const Args a) {
   const uint32_t vh = blockIdx.x, seq = blockIdx.y;
   const uint32_t kh = vh / a.group;
   float *S = a.state + (size_t(seq) * a.value_heads + vh) * DK * DV;
+  // The state streams into L2 while the kernel ahead still runs (a prefetch
+  // never changes what a later load returns): one 512-byte row per thread.
+  if (threadIdx.x < DK)
+    prefetch_l2(S + size_t(threadIdx.x) * DV, DV * 4);
+  pdl_enter();
 
   float4 s[R];
 #pragma unroll
@@ -134,7 +138,6 @@ __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v128(const Args a) {
 // Grid (Hv * dv / 32, batch), 256 threads; dk multiple of 32, <= 128.
 template <int DK>
 __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v32(const Args a) {
-  pdl_enter();
   constexpr int R = DK / 32;  // row passes per thread
   constexpr int DV = 128, kCols = 32;
   __shared__ float4 red_pred[kRecWarps][8];
@@ -145,6 +148,12 @@ __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v32(const Args a) {
   const uint32_t seq = blockIdx.y, kh = vh / a.group;
   const uint32_t col = blk * kCols + 4 * cg;  // this lane's first column within the head
   float *S = a.state + (size_t(seq) * a.value_heads + vh) * DK * DV;
+  // This block's state into L2 while the kernel ahead still runs (a prefetch
+  // never changes what a later load returns): one 128-byte row segment per
+  // thread.
+  if (threadIdx.x < DK)
+    prefetch_l2(S + size_t(threadIdx.x) * DV + blk * kCols, kCols * 4);
+  pdl_enter();
   auto row_of = [&](int p) { return warp * 4 + rs + 32 * p; };
 
   float4 s[R];

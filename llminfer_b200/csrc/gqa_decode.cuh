@@ -62,6 +62,7 @@ struct Partition {
   uint32_t max_span;          // units a worker can touch
   uint32_t workers;
   uint32_t heads;             // kv heads served by one worker
+  uint32_t prefetch_tiles;    // tiles a worker warms L2 with before it waits (<= 16)
 };
 
 __host__ __device__ inline uint32_t first_unit(const Partition &pt, uint32_t worker) {
@@ -88,7 +89,46 @@ struct Args {
   uint32_t kv_heads, group, head_dim, keys;  // keys = past + 1
   uint32_t record_floats;
   float scale_log2;      // log2(e) / sqrt(D)
+  // The step's KvAppend folded into the op (each may be null): the new K
+  // and V rows [batch][kv_heads][D], `new_stride` halves between sequences.
+  // The partial pass reads key keys - 1 from them, and the merge writes them
+  // into the caches' row keys - 1, which no kernel of the op reads.
+  const __half *k_new, *v_new;
+  size_t new_stride;
+  uint32_t batch;
 };
+
+// Key `key`'s row of K (value false) or V for sequence `seq`, from `head_off`
+// halves into the row: the step's new row when the caller passed it, else the
+// cache's.
+__device__ __forceinline__ const __half *kv_row(const Args &a, bool value, uint32_t seq,
+                                                uint32_t key, size_t head_off) {
+  const __half *fresh = value ? a.v_new : a.k_new;
+  if (fresh != nullptr && key + 1 == a.keys)
+    return fresh + seq * a.new_stride + head_off;
+  return (value ? a.v : a.k) + seq * a.cache_stride + size_t(key) * a.kv_heads * a.head_dim +
+         head_off;
+}
+
+// L2 warm-up of a CTA worker's first key tiles, issued before
+// wait_primary(): the cache rows are read-only to the kernels ahead in a
+// decode step except the newest, and a prefetch never changes what a later
+// load returns, so the first tiles stream in while the kernel ahead (the
+// appends, the previous layer) still runs.
+//
+// Tile t of units that are (sequence, kv head) pairs: one row of D halves
+// per key and head; lane 16 (V ? 1 : 0) + r takes key row r.
+template <int D>
+__device__ __forceinline__ void prefetch_head_rows(const Args &a, uint32_t t, int lane) {
+  const uint32_t tpu = a.pt.tiles_per_unit;
+  const uint32_t unit = t / tpu, key0 = (t % tpu) * kTileKeys;
+  const uint32_t seq = unit / a.kv_heads, kvh = unit % a.kv_heads;
+  const uint32_t row = uint32_t(lane & 15);
+  if (key0 + row >= a.keys)
+    return;
+  const __half *base = lane < 16 ? a.k : a.v;
+  prefetch_l2(base + seq * a.cache_stride + (size_t(key0 + row) * a.kv_heads + kvh) * D, D * 2);
+}
 
 // One warp's tensor-core state for one unit: the group's queries as B
 // fragments, the running max / sum for its two heads (N columns
@@ -228,11 +268,11 @@ __global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
   volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(empty + STAGES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Partition pt = a.pt;  // heads == HKV, units = sequences
-  pdl_enter();  // before the first global read
   const uint32_t worker = blockIdx.x;
   const uint32_t total = pt.units * pt.tiles_per_unit;
   const uint32_t begin = min(total, worker * pt.tiles_per_worker);
   const uint32_t end = min(total, begin + pt.tiles_per_worker);
+  pdl_enter();  // before the first global read
   if (begin >= end)
     return;  // uniform over the CTA
   if (threadIdx.x == 0) {
@@ -265,7 +305,7 @@ __global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
       __syncwarp();
       const uint32_t row = lane & 15;
       const uint32_t key = key0 + min(row, valid - 1);
-      const __half *src = (lane < 16 ? a.k : a.v) + seq * a.cache_stride + size_t(key) * HKV * D;
+      const __half *src = kv_row(a, lane >= 16, seq, key, 0);
       uint8_t *dst = smem + s * Shape::kStageBytes + (lane < 16 ? 0 : Shape::kTileBytes) +
                      row * Shape::kRowStride;
       bulk_g2s(dst, src, Shape::kRowBytes, &full[s], policy);
@@ -332,7 +372,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
       reinterpret_cast<uint64_t *>(smem + WARPS * STAGES * Shape::kStageBytes) + warp * STAGES;
 
   const Partition pt = a.pt;
-  pdl_enter();  // before the first global read
   // heads == 1: this warp is a worker; otherwise the CTA is, and this warp
   // serves kv head `warp` of each sequence in the CTA's range.
   const bool grouped = pt.heads > 1;
@@ -341,6 +380,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
   const uint32_t total = pt.units * pt.tiles_per_unit;
   const uint32_t begin = min(total, worker * pt.tiles_per_worker);
   const uint32_t end = min(total, begin + pt.tiles_per_worker);
+  pdl_enter();  // before the first global read
   if (begin >= end || (grouped && my_head >= pt.heads))
     return;  // warps are independent: no CTA-wide barrier below
 
@@ -367,8 +407,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
     __syncwarp();
     const uint32_t row = lane & 15;
     const uint32_t key = key0 + min(row, valid - 1);
-    const __half *src = (lane < 16 ? a.k : a.v) + seq * a.cache_stride +
-                        (size_t(key) * a.kv_heads + kvh) * D;
+    const __half *src = kv_row(a, lane >= 16, seq, key, size_t(kvh) * D);
     uint8_t *dst = stages + stage * Shape::kStageBytes + (lane < 16 ? 0 : Shape::kTileBytes) +
                    row * Shape::kRowStride;
     bulk_g2s(dst, src, Shape::kRowBytes, &bars[stage], policy);
@@ -452,11 +491,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma_cta(const Args a) {
   float *states = reinterpret_cast<float *>(smem + CtaShape::kStatesOffset);
 
   const Partition pt = a.pt;  // heads == 1, workers are CTAs
-  pdl_enter();  // before the first global read
   const uint32_t worker = blockIdx.x;
   const uint32_t total = pt.units * pt.tiles_per_unit;
   const uint32_t begin = min(total, worker * pt.tiles_per_worker);
   const uint32_t end = min(total, begin + pt.tiles_per_worker);
+  // The warps take the range's tiles in turn: each warms its own first ones.
+  for (uint32_t t = begin + warp; t < min(end, begin + pt.prefetch_tiles); t += WARPS)
+    prefetch_head_rows<D>(a, t, lane);
+  pdl_enter();  // before the first global read (prefetches aside)
   if (begin >= end)
     return;  // uniform over the CTA
 
@@ -496,8 +538,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma_cta(const Args a) {
     __syncwarp();
     const uint32_t row = lane & 15;
     const uint32_t key = key0 + min(row, valid - 1);
-    const __half *src = (lane < 16 ? a.k : a.v) + seq * a.cache_stride +
-                        (size_t(key) * a.kv_heads + kvh) * D;
+    const __half *src = kv_row(a, lane >= 16, seq, key, size_t(kvh) * D);
     uint8_t *dst = stages + stage * Shape::kStageBytes + (lane < 16 ? 0 : Shape::kTileBytes) +
                    row * Shape::kRowStride;
     bulk_g2s(dst, src, Shape::kRowBytes, &bars[stage], policy);
@@ -692,6 +733,8 @@ constexpr int kMergeMaxGroup = 64;
 constexpr int kMergeMaxPerLane = 16;  // head_dim <= 512
 constexpr int kMergeRound = 4;        // records per round of float4 loads
 constexpr int kMergeSmemRecords = 512;  // records per unit whose weights are staged in smem
+constexpr int kMergeHeld = 16;  // records per lane group held in registers by the one-round path
+constexpr int kMergeAppendPerThread = 4;  // head_dim <= 512 over kMergeThreads threads
 
 __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   launch_dependents();
@@ -708,9 +751,14 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
       uint32_t((uint64_t(unit + 1) * pt.tiles_per_unit - 1) / pt.tiles_per_worker);
   const uint32_t n = w_hi - w_lo + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  auto record = [&](uint32_t i) {
-    return a.records + record_index(pt, w_lo + i, unit, head) * a.record_floats;
-  };
+  // Record i of the unit is worker w_lo + i's.  Every worker after w_lo
+  // starts inside this unit (w * tiles_per_worker > unit * tiles_per_unit),
+  // so its record is slot 0 of its span: the records from i = 1 on are
+  // evenly spaced, and only record 0 needs the general index.
+  const float *rec0 = a.records + record_index(pt, w_lo, unit, head) * a.record_floats;
+  const float *rec1 = a.records + (uint64_t(w_lo) * pt.max_span * pt.heads + head) * a.record_floats;
+  const size_t rstep = size_t(pt.max_span) * pt.heads * a.record_floats;
+  auto record = [&](uint32_t i) { return i == 0 ? rec0 : rec1 + i * rstep; };
   // float4 path: every head's output row starts on a 16-byte boundary
   // (records are, and 2G and D are multiples of 4), the slice is whole
   // float4 columns and the fp16 output rows start on an 8-byte boundary.
@@ -723,8 +771,91 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   __shared__ float staged[kMergeThreads / 32][2][kMergeSmemRecords];
   const bool stage = n <= uint32_t(kMergeSmemRecords);
   wait_primary();
+  // The folded KvAppend: this CTA's share is columns [d0, d1) of kv head
+  // kvh of sequence seq's new K and V rows, loaded here and stored at the end
+  // (the load's latency hides under the merge).
+  const bool append = a.k_new != nullptr || a.v_new != nullptr;
+  const size_t new_at = seq * a.new_stride + size_t(kvh) * D;
+  const size_t cache_at = seq * a.cache_stride + (size_t(a.keys - 1) * a.kv_heads + kvh) * D;
+  __half k_row[kMergeAppendPerThread], v_row[kMergeAppendPerThread];
+#pragma unroll
+  for (int r = 0; r < kMergeAppendPerThread; ++r) {
+    const uint32_t d = d0 + threadIdx.x + r * kMergeThreads;
+    k_row[r] = append && a.k_new && d < d1 ? a.k_new[new_at + d] : __half();
+    v_row[r] = append && a.v_new && d < d1 ? a.v_new[new_at + d] : __half();
+  }
   __half *out = a.out + (size_t(seq) * a.kv_heads * G + kvh * G) * D;
-  for (uint32_t h = warp; h < G; h += kMergeThreads / 32) {
+  // The slice's float4 columns, and the lane groups that sum interleaved
+  // records (F a power of two below 32).
+  const uint32_t F = (d1 - d0) / 4;
+  const bool grouped_lanes = vec && F < 32 && (F & (F - 1)) == 0;
+  const uint32_t R = grouped_lanes ? 32 / F : 1;
+  const uint32_t g = grouped_lanes ? lane / F : 0, f = grouped_lanes ? lane % F : lane;
+  const uint32_t c0 = d0 / 4;
+  // Few records (at most 4 per lane, kMergeHeld per lane group): one round
+  // of loads fetches every max, sum and output column the warp needs, so
+  // the merge costs one trip to the partial pass's records in L2 instead of
+  // one per dependent step.
+  const bool one_round = grouped_lanes && n <= 128u && n <= R * uint32_t(kMergeHeld);
+  for (uint32_t h = warp; one_round && h < G; h += kMergeThreads / 32) {
+    float *sm_w = staged[warp][0];
+    float mv[4], lv[4];
+    float4 v[kMergeHeld];
+#pragma unroll
+    for (int s4 = 0; s4 < 4; ++s4) {
+      const uint32_t i = lane + 32 * s4;
+      const float *r = record(min(i, n - 1));
+      mv[s4] = i < n ? r[h] : -INFINITY;
+      lv[s4] = i < n ? r[G + h] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kMergeHeld; ++j) {
+      const uint32_t i = g + R * j;
+      v[j] = i < n ? reinterpret_cast<const float4 *>(record(i) + 2 * G + h * D)[c0 + f]
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float top = fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3]));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+      top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, off));
+    float sum = 0.f;
+#pragma unroll
+    for (int s4 = 0; s4 < 4; ++s4) {
+      const uint32_t i = lane + 32 * s4;
+      if (i < n) {
+        const float w = fast_exp2(mv[s4] - top);
+        sm_w[i] = w;
+        sum = fmaf(lv[s4], w, sum);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+      sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    __syncwarp();
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < kMergeHeld; ++j) {
+      const uint32_t i = g + R * j;
+      const float w = i < n ? sm_w[i] : 0.f;
+      acc.x = fmaf(v[j].x, w, acc.x);
+      acc.y = fmaf(v[j].y, w, acc.y);
+      acc.z = fmaf(v[j].z, w, acc.z);
+      acc.w = fmaf(v[j].w, w, acc.w);
+    }
+    for (uint32_t off = F; off < 32; off <<= 1) {
+      acc.x += __shfl_xor_sync(0xffffffffu, acc.x, int(off));
+      acc.y += __shfl_xor_sync(0xffffffffu, acc.y, int(off));
+      acc.z += __shfl_xor_sync(0xffffffffu, acc.z, int(off));
+      acc.w += __shfl_xor_sync(0xffffffffu, acc.w, int(off));
+    }
+    __syncwarp();  // the staged weights are rewritten for the warp's next head
+    if (g == 0) {
+      const float inv = 1.f / sum;
+      *reinterpret_cast<uint2 *>(out + h * D + 4 * (c0 + f)) =
+          make_uint2(pack_half2(acc.x * inv, acc.y * inv), pack_half2(acc.z * inv, acc.w * inv));
+    }
+  }
+  for (uint32_t h = warp; !one_round && h < G; h += kMergeThreads / 32) {
     float *sm_w = staged[warp][0], *sm_l = staged[warp][1];
     float top = -INFINITY, sum = 0.f, w_own = 0.f;
     if (stage) {
@@ -777,13 +908,6 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
     };
     const float inv = 1.f / sum;
     if (vec) {
-      const uint32_t F = (d1 - d0) / 4;  // float4 columns in the slice
-      // Record groups of lanes when F is a power of two below 32 (the
-      // groups' sums then combine by xor shuffles); else one group.
-      const bool grouped_lanes = F < 32 && (F & (F - 1)) == 0;
-      const uint32_t R = grouped_lanes ? 32 / F : 1;
-      const uint32_t g = grouped_lanes ? lane / F : 0, f = grouped_lanes ? lane % F : lane;
-      const uint32_t c0 = d0 / 4;
       float4 acc[kMergeMaxPerLane / 4];
 #pragma unroll
       for (int k = 0; k < kMergeMaxPerLane / 4; ++k)
@@ -875,6 +999,18 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
         const uint32_t d = d0 + lane + 32 * k;
         if (d < d1)
           out[h * D + d] = __float2half_rn(acc[k] * inv);
+      }
+    }
+  }
+  if (append) {
+#pragma unroll
+    for (int r = 0; r < kMergeAppendPerThread; ++r) {
+      const uint32_t d = d0 + threadIdx.x + r * kMergeThreads;
+      if (d < d1) {
+        if (a.k_new)
+          const_cast<__half *>(a.k)[cache_at + d] = k_row[r];
+        if (a.v_new)
+          const_cast<__half *>(a.v)[cache_at + d] = v_row[r];
       }
     }
   }

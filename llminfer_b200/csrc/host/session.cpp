@@ -279,6 +279,9 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
     }
     return LLMI_OK;
   };
+  // A decode step's KvAppend rows, held for the layer's CausalGqa, which
+  // appends them in its own partial pass (llmi_cuda_gqa_decode_append).
+  const uint16_t *foldK = nullptr, *foldV = nullptr;
   for (size_t i = 0; i < ops.size(); ++i) {
     const Op &op = ops[i];
     if (proj && (i == 0 || ops[i - 1].layer != op.layer))
@@ -302,7 +305,14 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
       launchedAny = true;
       if (proj)
         skip = 1;  // normRope wrote the keys
-      else
+      count = 2;
+      if (tokens == 1 && i + 1 < ops.size() && ops[i + 1].kind == OpKind::CausalGqa &&
+          ops[i + 1].layer == op.layer) {
+        foldK = proj ? nullptr : static_cast<const uint16_t *>(x.k);
+        foldV = static_cast<const uint16_t *>(x.v);
+        break;
+      }
+      if (!proj)
         e = llmi_cuda_cache_append(&p, B, static_cast<const uint16_t *>(x.k), inStride,
                                    static_cast<uint16_t *>(s.keys[op.layer]), cacheStride,
                                    s.stream);
@@ -310,7 +320,6 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
         e = llmi_cuda_cache_append(&p, B, static_cast<const uint16_t *>(x.v), inStride,
                                    static_cast<uint16_t *>(s.values[op.layer]), cacheStride,
                                    s.stream);
-      count = 2;
       break;
     }
     case OpKind::CausalGqa: {
@@ -321,6 +330,14 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
                                   static_cast<const uint16_t *>(s.keys[op.layer]),
                                   static_cast<const uint16_t *>(s.values[op.layer]), cacheStride,
                                   static_cast<uint16_t *>(x.out), s.stream);
+      } else if (foldK || foldV) {
+        e = llmi_cuda_gqa_decode_append(
+            &p, B, static_cast<const uint16_t *>(x.q), foldK, foldV,
+            size_t(c.kvHeads) * c.headDim, static_cast<uint16_t *>(s.keys[op.layer]),
+            static_cast<uint16_t *>(s.values[op.layer]), cacheStride,
+            static_cast<uint16_t *>(x.out), s.workspace, s.workspaceBytes, s.stream);
+        foldK = foldV = nullptr;
+        count = 2;
       } else {
         e = llmi_cuda_gqa_decode(&p, B, static_cast<const uint16_t *>(x.q),
                                  static_cast<const uint16_t *>(s.keys[op.layer]),

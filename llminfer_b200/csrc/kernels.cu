@@ -150,8 +150,24 @@ constexpr int kCtaStages256 = 1, kCtaStages128 = 2, kCtaStages64 = 4;
 // the latency of the tile math.
 constexpr int kCtaWarps256 = 8, kCtaWarps128 = kWarps128, kCtaWarps64 = kWarps64;
 constexpr int kRowStages = 3;
+// Bytes of cache rows the CTA workers of the decode partial pass warm L2
+// with, over the whole grid, before waiting for the kernel ahead of them
+// (16 MB: about two tiles per warp at the shapes that use them, and well
+// inside L2).  The whole-row kinds warm nothing: each CTA puts three 64 KB
+// tiles in flight at once, and prefetches beside them only competed with
+// those copies (a B=2, 16/4-head step took 1.5 us longer with them).
+constexpr uint64_t kDecodePrefetchBytes = 16ull << 20;
 // DeltaUpdate calls with at least this many tokens use the chunked kernel.
 constexpr uint32_t kChunkedMinTokens = 16;
+
+// Tiles per CTA worker to warm L2 with: at most 16 and at most
+// kDecodePrefetchBytes over the grid.  `tile_bytes`: the K and V rows a
+// worker reads for one tile.
+uint32_t prefetch_tiles(const DecodePlan &plan, uint64_t tile_bytes) {
+  const uint64_t round = std::max<uint64_t>(1, uint64_t(plan.grid) * tile_bytes);
+  return uint32_t(std::min<uint64_t>({uint64_t(plan.pt.tiles_per_worker), 16ull,
+                                      kDecodePrefetchBytes / round}));
+}
 
 // Picks the decode kernels and the work partition.  The tensor-core partial
 // pass needs 16-byte aligned operands (bulk copies) and a supported shape;
@@ -247,6 +263,8 @@ int plan_decode(const llmi_gqa_params &p, unsigned batch, bool aligned, const De
     plan.pt.max_span = std::min<uint32_t>(part_units, (tpw + tpu - 1) / tpu + 1);
     plan.pt.workers = plan.grid * per_cta;
     plan.pt.heads = grouped ? p.kvHeads : 1u;
+    if (plan.cta_workers)
+      plan.pt.prefetch_tiles = prefetch_tiles(plan, 2ull * decode::kTileKeys * D * 2);
   } else {
     if (D > 512)
       return fail(LLMI_UNSUPPORTED, "decode: head_dim %u above 512", D);
@@ -596,16 +614,22 @@ extern "C" size_t llmi_cuda_gqa_decode_workspace(const llmi_gqa_params *p, unsig
   return std::max(a ? 0 : fast.workspace, b ? 0 : simt.workspace);
 }
 
-extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, const uint16_t *q,
-                                    const uint16_t *k_cache, const uint16_t *v_cache,
-                                    size_t cache_stride, uint16_t *out, void *workspace,
-                                    size_t workspace_bytes, void *stream) {
-  clear_error();
-  if (int s = check_gqa(p, batch, q, k_cache, v_cache, cache_stride, out))
-    return s;
-  if (p->tokens != 1)
-    return fail(LLMI_UNSUPPORTED, "decode: %u tokens; the decode path takes one token (use prefill)",
-                p->tokens);
+namespace {
+
+// A step's new K and V rows for the decode pass to append (each may be null).
+struct NewRows {
+  const uint16_t *k = nullptr, *v = nullptr;
+  size_t stride = 0;  // halves between sequences
+};
+
+// gqaScores + gqaSoftmax, with the step's KvAppend folded in when `fresh`
+// holds rows and the partial pass is a tensor-core one: that pass reads the
+// new rows from `fresh` and the merge writes them into the caches.
+// Otherwise the appends run first as their own launches.  Arguments checked.
+int gqa_decode_run(const llmi_gqa_params *p, unsigned batch, const uint16_t *q,
+                   const uint16_t *k_cache, const uint16_t *v_cache, size_t cache_stride,
+                   uint16_t *out, void *workspace, size_t workspace_bytes, void *stream,
+                   NewRows fresh) {
   if (!workspace)
     return fail(LLMI_INVALID_ARGUMENT, "decode: null workspace");
   DeviceInfo dev;
@@ -621,6 +645,23 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
                 workspace_bytes, plan.workspace);
   if (!aligned16(workspace))
     return fail(LLMI_INVALID_ARGUMENT, "decode: workspace must be 16-byte aligned");
+  if (fresh.k || fresh.v) {
+    const bool fold = plan.kind != DecodePlan::Simt && (!fresh.k || aligned16(fresh.k)) &&
+                      (!fresh.v || aligned16(fresh.v)) && (batch == 1 || fresh.stride % 8 == 0);
+    if (!fold) {
+      const unsigned row = p->kvHeads * p->headDim;
+      llmi_cache_params c{row, p->past * row};
+      const uint16_t *rows[2] = {fresh.k, fresh.v};
+      const uint16_t *caches[2] = {k_cache, v_cache};
+      for (int i = 0; i < 2; ++i)
+        if (rows[i])
+          if (int s = llmi_cuda_cache_append(&c, batch, rows[i], fresh.stride,
+                                             const_cast<uint16_t *>(caches[i]), cache_stride,
+                                             stream))
+            return s;
+      fresh = NewRows{};
+    }
+  }
 
   decode::Args a;
   a.q = reinterpret_cast<const __half *>(q);
@@ -636,6 +677,10 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
   a.keys = p->past + 1;
   a.record_floats = plan.record_floats;
   a.scale_log2 = kLog2e / std::sqrt(float(p->headDim));
+  a.k_new = reinterpret_cast<const __half *>(fresh.k);
+  a.v_new = reinterpret_cast<const __half *>(fresh.v);
+  a.new_stride = fresh.stride;
+  a.batch = batch;
   cudaStream_t s = as_stream(stream);
   int status = LLMI_OK;
   switch (plan.kind) {
@@ -675,6 +720,43 @@ extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, co
     slices *= 2;
   return launch_dependent("gqaSoftmax (decode merge)", decode::merge, dim3(units, slices),
                           dim3(decode::kMergeThreads), 0, s, a);
+}
+
+}  // namespace
+
+extern "C" int llmi_cuda_gqa_decode(const llmi_gqa_params *p, unsigned batch, const uint16_t *q,
+                                    const uint16_t *k_cache, const uint16_t *v_cache,
+                                    size_t cache_stride, uint16_t *out, void *workspace,
+                                    size_t workspace_bytes, void *stream) {
+  clear_error();
+  if (int s = check_gqa(p, batch, q, k_cache, v_cache, cache_stride, out))
+    return s;
+  if (p->tokens != 1)
+    return fail(LLMI_UNSUPPORTED, "decode: %u tokens; the decode path takes one token (use prefill)",
+                p->tokens);
+  return gqa_decode_run(p, batch, q, k_cache, v_cache, cache_stride, out, workspace,
+                        workspace_bytes, stream, NewRows{});
+}
+
+extern "C" int llmi_cuda_gqa_decode_append(const llmi_gqa_params *p, unsigned batch,
+                                           const uint16_t *q, const uint16_t *k_new,
+                                           const uint16_t *v_new, size_t new_stride,
+                                           uint16_t *k_cache, uint16_t *v_cache,
+                                           size_t cache_stride, uint16_t *out, void *workspace,
+                                           size_t workspace_bytes, void *stream) {
+  clear_error();
+  if (int s = check_gqa(p, batch, q, k_cache, v_cache, cache_stride, out))
+    return s;
+  if (p->tokens != 1)
+    return fail(LLMI_UNSUPPORTED, "decode_append: %u tokens; the decode path takes one token",
+                p->tokens);
+  const uint64_t row = uint64_t(p->kvHeads) * p->headDim;
+  if (uint64_t(p->past) * row + row > UINT32_MAX)
+    return fail(LLMI_UNSUPPORTED, "decode_append: cache offsets exceed 32 bits");
+  if (batch > 1 && (k_new || v_new) && new_stride < row)
+    return fail(LLMI_INVALID_ARGUMENT, "decode_append: new rows of sequences overlap");
+  return gqa_decode_run(p, batch, q, k_cache, v_cache, cache_stride, out, workspace,
+                        workspace_bytes, stream, NewRows{k_new, v_new, new_stride});
 }
 
 // ---- decode without a caller workspace ------------------------------------------------

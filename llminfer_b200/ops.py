@@ -99,6 +99,43 @@ def gqa_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pa
     return out
 
 
+def gqa_decode_append(q: torch.Tensor, k_new: torch.Tensor | None, v_new: torch.Tensor | None,
+                      k_cache: torch.Tensor, v_cache: torch.Tensor, past: int,
+                      out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                      stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """KvAppend + decode in one pass: writes k_new / v_new [B, 1, Hkv, D] (None: that
+    row is already in the cache) into cache row `past`, then decodes over rows
+    [0, past] like gqa_decode."""
+    for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _need(t, torch.float16, n)
+    p = _gqa_params(q, k_cache, past)
+    row = p.kvHeads * p.headDim
+    new_stride = 0
+    for t, n in ((k_new, "k_new"), (v_new, "v_new")):
+        if t is None:
+            continue
+        _need(t, torch.float16, n)
+        if t.shape != (q.shape[0], 1, p.kvHeads, p.headDim):
+            raise ValueError(f"{n} must be [B, 1, Hkv, D]")
+        if new_stride and t.stride(0) != new_stride:
+            raise ValueError("k_new and v_new must share one sequence stride")
+        new_stride = t.stride(0)
+    if past + 1 > k_cache.shape[1]:
+        raise ValueError("gqa_decode_append: the cache is full")
+    if workspace is None:
+        n = decode_workspace_bytes(q.shape[0], p.queryHeads, p.kvHeads, p.headDim, past)
+        workspace = torch.empty(n, dtype=torch.uint8, device=q.device)
+    out = torch.empty_like(q) if out is None else out
+    _need(out, torch.float16, "out")
+    check(lib.llmi_cuda_gqa_decode_append(
+        ctypes.byref(p), q.shape[0], q.data_ptr(),
+        k_new.data_ptr() if k_new is not None else None,
+        v_new.data_ptr() if v_new is not None else None, new_stride or row,
+        k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0), out.data_ptr(),
+        workspace.data_ptr(), workspace.numel(), _stream(stream)))
+    return out
+
+
 def delta_workspace_bytes(batch: int, tokens: int, key_heads: int, key_dim: int,
                           value_heads: int, value_dim: int) -> int:
     """Scratch bytes of delta_update's chunk-parallel form (0 if the call does not use it)."""

@@ -128,6 +128,39 @@ def test_decode_and_prefill_agree_on_one_token():
     assert max_abs <= 4e-3 and rel <= 2e-3
 
 
+@pytest.mark.parametrize("batch,past,hq,hkv,d", [
+    (3, 700, 16, 4, 256),    # whole rows, 2 KiB (partial_rows<256, 4>)
+    (200, 20, 16, 4, 256),   # more sequences than CTAs: a CTA writes several rows
+    (2, 515, 8, 2, 256),     # whole rows, 1 KiB (partial_rows<256, 2>)
+    (2, 333, 16, 8, 128),    # whole rows (partial_rows<128, 8>)
+    (3, 260, 16, 8, 64),     # grouped warps (partial_mma<64>)
+    (8, 2000, 4, 1, 256),    # CTA workers (partial_mma_cta<256>)
+    (3, 500, 12, 3, 128),    # CTA workers, 3 kv heads
+    (2, 100, 8, 2, 96),      # CUDA-core pass: the appends run as their own launches
+    (1, 0, 16, 4, 256),      # the new row is the only key
+])
+@pytest.mark.parametrize("keys_given", [True, False])
+def test_decode_append_matches_separate_calls(batch, past, hq, hkv, d, keys_given):
+    """llmi_cuda_gqa_decode_append against cacheAppend x2 + gqa_decode: the same
+    output bits and the same caches (k_new None: the key row is already written)."""
+    q, k, v = _inputs.gqa_case(batch, 1, past, hq, hkv, d, capacity=past + 3, seed=40 + past)
+    kn = dev(_inputs.half_normal(1, 41, (batch, 1, hkv, d)))
+    vn = dev(_inputs.half_normal(1, 42, (batch, 1, hkv, d)))
+    kc_a, vc_a = dev(k), dev(v)
+    kc_b, vc_b = kc_a.clone(), vc_a.clone()
+    if not keys_given:
+        ops.cache_append(kn, kc_b, past)  # written beforehand (as normRope does)
+    ops.cache_append(kn, kc_a, past)
+    ops.cache_append(vn, vc_a, past)
+    want = ops.gqa_decode(dev(q), kc_a, vc_a, past, out=nan_like(dev(q)))
+    got = ops.gqa_decode_append(dev(q), kn if keys_given else None, vn, kc_b, vc_b, past,
+                                out=nan_like(dev(q)))
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    assert torch.equal(kc_b.view(torch.int16), kc_a.view(torch.int16))
+    assert torch.equal(vc_b.view(torch.int16), vc_a.view(torch.int16))
+
+
 def test_decode_rejects_small_workspace():
     q, k, v = _inputs.gqa_case(2, 1, 100, 16, 4, 256, seed=13)
     small = torch.empty(256, dtype=torch.uint8, device="cuda")
