@@ -14,6 +14,7 @@ on the CPU before timing).  Prints one JSON object.
   python -m llminfer_b200.kernel_bench append  --batch 64 --tokens 1 --past 4096
   python -m llminfer_b200.kernel_bench rope    --batch 16 --tokens 8192 --past 0
   python -m llminfer_b200.kernel_bench deltaprep --batch 16 --tokens 8192
+  python -m llminfer_b200.kernel_bench step --batch 2 --past 8320 --capacity 8448
   python -m llminfer_b200.kernel_bench traffic --csv launches.csv --workload decode \
       --batch 64 --past 4096 --capacity 8192 [--out profiles/traffic_c2_decode.jsonl]
 """
@@ -391,10 +392,68 @@ def traffic(args):
     return lines
 
 
+def bench_step(args):
+    """One C5 decode step at `--batch` sequences, and its parts, each captured
+    into a CUDA graph and replayed (device time per replay): 8 GQA layers (KvAppend
+    + decode, through llmi_cuda_gqa_decode_append as the session issues them, and
+    as three separate calls) and 24 recurrent DeltaNet layers, interleaved as in
+    the hybrid stack (three DeltaNet layers, then one GQA layer)."""
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    B, (Hq, Hkv), D, P, cap = args.batch, args.heads, args.dim, args.past, args.capacity
+    (Hk, Hv), (dk, dv) = args.delta_heads, args.delta_dims
+    layers, dlayers = args.layers, 3 * args.layers
+    kc = [torch.randn(B, cap, Hkv, D, generator=g, device="cuda").half() for _ in range(layers)]
+    vc = [torch.randn(B, cap, Hkv, D, generator=g, device="cuda").half() for _ in range(layers)]
+    q = torch.randn(B, 1, Hq, D, generator=g, device="cuda").half()
+    kn = torch.randn(B, 1, Hkv, D, generator=g, device="cuda").half()
+    vn = torch.randn(B, 1, Hkv, D, generator=g, device="cuda").half()
+    out = torch.empty_like(q)
+    ws = torch.empty(ops.decode_workspace_bytes(B, Hq, Hkv, D, P), dtype=torch.uint8,
+                     device="cuda")
+    nrm = torch.nn.functional.normalize
+    dq = nrm(torch.randn(B, 1, Hk, dk, generator=g, device="cuda"), dim=-1).reshape(B, 1, -1)
+    dkk = nrm(torch.randn(B, 1, Hk, dk, generator=g, device="cuda"), dim=-1).reshape(B, 1, -1)
+    dvv = torch.randn(B, 1, Hv * dv, generator=g, device="cuda").half()
+    beta = torch.rand(B, 1, Hv, generator=g, device="cuda")
+    decay = torch.rand(B, 1, Hv, generator=g, device="cuda") * 0.5 + 0.5
+    states = [torch.randn(B, Hv, dk, dv, generator=g, device="cuda") * 0.02
+              for _ in range(dlayers)]
+    dout = torch.empty_like(dvv)
+
+    def gqa(l, folded=True):
+        if folded:
+            ops.gqa_decode_append(q, kn, vn, kc[l], vc[l], P, out=out, workspace=ws)
+        else:
+            ops.cache_append(kn, kc[l], P)
+            ops.cache_append(vn, vc[l], P)
+            ops.gqa_decode(q, kc[l], vc[l], P, out=out, workspace=ws)
+
+    def rec(l):
+        ops.delta_update(dq, dkk, dvv, beta, decay, states[l], out=dout, workspace=False)
+
+    def step(folded=True):
+        for i in range(layers):
+            for j in range(3):
+                rec(3 * i + j)
+            gqa(i, folded)
+
+    reps = max(args.samples, 5)
+    us = lambda fn, n=1: round(time_graph(fn, reps) * 1000 / n, 2)
+    return {"op": "decode step", "batch": B, "heads": [Hq, Hkv], "dim": D, "past": P,
+            "capacity": cap, "gqa_layers": layers, "delta_layers": dlayers,
+            "delta_heads": [Hk, Hv], "delta_dims": [dk, dv],
+            "us_step": us(step), "us_step_separate_appends": us(lambda: step(False)),
+            "us_gqa_layer": us(lambda: [gqa(l) for l in range(layers)], layers),
+            "us_gqa_layer_separate_appends":
+                us(lambda: [gqa(l, False) for l in range(layers)], layers),
+            "us_delta_layer": us(lambda: [rec(l) for l in range(dlayers)], dlayers),
+            "timing": "each part captured into one CUDA graph, replayed back to back"}
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     p.add_argument("op", choices=["decode", "prefill", "delta", "append", "rope", "deltaprep",
-                                  "traffic"])
+                                  "step", "traffic"])
     p.add_argument("--csv", help="traffic: ncu --csv file of gpu__time_duration.sum, "
                                  "dram__bytes_read.sum, dram__bytes_write.sum")
     p.add_argument("--workload", choices=["decode", "prefill", "delta"], default="decode",
@@ -415,6 +474,8 @@ def main(argv=None):
     p.add_argument("--no-check", action="store_true")
     p.add_argument("--graph", action="store_true",
                    help="decode/prefill: also time the call replayed from a CUDA graph")
+    p.add_argument("--layers", type=int, default=8,
+                   help="step: GQA layers (three DeltaNet layers each)")
     p.add_argument("--no-scratch", action="store_true",
                    help="delta: the entry point without scratch (llmi_cuda_delta_update)")
     args = p.parse_args(argv)
@@ -436,6 +497,8 @@ def main(argv=None):
         res = bench_rope(args)
     elif args.op == "deltaprep":
         res = bench_deltaprep(args)
+    elif args.op == "step":
+        res = bench_step(args)
     else:
         res = bench_append(args)
     ops.poll_error()
