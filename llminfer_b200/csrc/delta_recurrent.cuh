@@ -42,10 +42,10 @@ __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v128(const Args a) {
   const uint32_t vh = blockIdx.x, seq = blockIdx.y;
   const uint32_t kh = vh / a.group;
   float *S = a.state + (size_t(seq) * a.value_heads + vh) * DK * DV;
-  // The state streams into L2 while the kernel ahead still runs (a prefetch
-  // never changes what a later load returns): one 512-byte row per thread.
-  if (threadIdx.x < DK)
-    prefetch_l2(S + size_t(threadIdx.x) * DV, DV * 4);
+  // No L2 warm-up here (recurrent_v32 has one): this form runs when many
+  // CTAs stream the state in waves, HBM-bound, and prefetches by the CTAs
+  // resident ahead of their wait only re-read lines the kernel ahead is
+  // about to write (1.8 % slower at C4).
   pdl_enter();
 
   float4 s[R];

@@ -98,18 +98,6 @@ struct Args {
   uint32_t batch;
 };
 
-// Key `key`'s row of K (value false) or V for sequence `seq`, from `head_off`
-// halves into the row: the step's new row when the caller passed it, else the
-// cache's.
-__device__ __forceinline__ const __half *kv_row(const Args &a, bool value, uint32_t seq,
-                                                uint32_t key, size_t head_off) {
-  const __half *fresh = value ? a.v_new : a.k_new;
-  if (fresh != nullptr && key + 1 == a.keys)
-    return fresh + seq * a.new_stride + head_off;
-  return (value ? a.v : a.k) + seq * a.cache_stride + size_t(key) * a.kv_heads * a.head_dim +
-         head_off;
-}
-
 // L2 warm-up of a CTA worker's first key tiles, issued before
 // wait_primary(): the cache rows are read-only to the kernels ahead in a
 // decode step except the newest, and a prefetch never changes what a later
@@ -291,25 +279,37 @@ __global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
     // value rows, each row [Hkv][D] with one bulk copy.  Rows past the end of
     // the cache range repeat the last valid row (masked to -inf).
     const uint64_t policy = policy_evict_first();
+    // The step's new row of this lane's K or V, when the caller folded the
+    // KvAppend in: it replaces the cache's row keys - 1.
+    const __half *fresh = lane < 16 ? a.k_new : a.v_new;
     uint32_t issued = 0;
+    // Tile t is keys [key0, key0 + 16) of sequence seq; both advance with t
+    // (no division per tile: the copies' issue is on the pipeline's path).
+    uint32_t seq = begin / tpu, key0 = (begin % tpu) * kTileKeys;
     for (uint32_t t = begin; t < end; ++t) {
       const uint32_t j = t - begin;
       const int s = j % STAGES;
       if (j >= STAGES &&
           !__all_sync(0xffffffffu, wait_or_abort(&empty[s], ((j / STAGES) - 1) & 1, abort)))
         break;
-      const uint32_t seq = t / tpu, key0 = (t % tpu) * kTileKeys;
       const uint32_t valid = min(uint32_t(kTileKeys), a.keys - key0);
       if (lane == 0)
         mbar_arrive_expect_tx(&full[s], 2 * kTileKeys * Shape::kRowBytes);
       __syncwarp();
       const uint32_t row = lane & 15;
       const uint32_t key = key0 + min(row, valid - 1);
-      const __half *src = kv_row(a, lane >= 16, seq, key, 0);
+      const __half *src = (lane < 16 ? a.k : a.v) + seq * a.cache_stride + size_t(key) * HKV * D;
+      if (fresh != nullptr && key + 1 == a.keys)
+        src = fresh + seq * a.new_stride;
       uint8_t *dst = smem + s * Shape::kStageBytes + (lane < 16 ? 0 : Shape::kTileBytes) +
                      row * Shape::kRowStride;
       bulk_g2s(dst, src, Shape::kRowBytes, &full[s], policy);
       issued = j + 1;
+      key0 += kTileKeys;
+      if (key0 >= a.keys) {
+        key0 = 0;
+        ++seq;
+      }
     }
     // Every issued copy lands before the CTA can exit (bounded).
     if (lane == 0)
@@ -324,10 +324,10 @@ __global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
   TileMath<D> math;
   uint32_t unit = 0xffffffffu;
   bool ok = true;
+  uint32_t u = begin / tpu, key0 = (begin % tpu) * kTileKeys;  // tile t, advanced with t
   for (uint32_t t = begin; t < end; ++t) {
     const uint32_t j = t - begin;
     const int s = j % STAGES;
-    const uint32_t u = t / tpu;
     if (u != unit) {
       if (unit != 0xffffffffu)
         math.flush(a.records + record_index(pt, worker, unit, h) * a.record_floats, a.group, lane);
@@ -339,11 +339,16 @@ __global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
       break;
     }
     const uint32_t kbase = smem_u32(smem + s * Shape::kStageBytes) + h * D * 2;
-    const uint32_t valid = min(uint32_t(kTileKeys), a.keys - (t % tpu) * kTileKeys);
+    const uint32_t valid = min(uint32_t(kTileKeys), a.keys - key0);
     math.tile(kbase, kbase + Shape::kTileBytes, Shape::kRowStride, valid, a.scale_log2, lane);
     __syncwarp();
     if (lane == 0)
       mbar_arrive(&empty[s]);
+    key0 += kTileKeys;
+    if (key0 >= a.keys) {
+      key0 = 0;
+      ++u;
+    }
   }
   if (ok)
     math.flush(a.records + record_index(pt, worker, unit, h) * a.record_floats, a.group, lane);
@@ -393,6 +398,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
 
   const uint64_t policy = policy_evict_first();
   const uint32_t tpu = pt.tiles_per_unit;
+  const __half *fresh = lane < 16 ? a.k_new : a.v_new;
 
   // Lanes 0-15 fetch the 16 key rows, lanes 16-31 the 16 value rows.  Rows
   // past the end of the cache range repeat the last valid row (their scores
@@ -407,7 +413,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma(const Args a) {
     __syncwarp();
     const uint32_t row = lane & 15;
     const uint32_t key = key0 + min(row, valid - 1);
-    const __half *src = kv_row(a, lane >= 16, seq, key, size_t(kvh) * D);
+    const __half *src = (lane < 16 ? a.k : a.v) + seq * a.cache_stride +
+                        (size_t(key) * a.kv_heads + kvh) * D;
+    if (fresh != nullptr && key + 1 == a.keys)  // the step's new row (folded KvAppend)
+      src = fresh + seq * a.new_stride + size_t(kvh) * D;
     uint8_t *dst = stages + stage * Shape::kStageBytes + (lane < 16 ? 0 : Shape::kTileBytes) +
                    row * Shape::kRowStride;
     bulk_g2s(dst, src, Shape::kRowBytes, &bars[stage], policy);
@@ -511,6 +520,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma_cta(const Args a) {
 
   const uint64_t policy = policy_evict_first();
   const uint32_t tpu = pt.tiles_per_unit;
+  const __half *fresh = lane < 16 ? a.k_new : a.v_new;  // the step's new rows, if folded
   const uint32_t G = a.group, F = a.record_floats;
   const uint32_t u_first = begin / tpu, u_last = (end - 1) / tpu;
 
@@ -538,7 +548,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1) partial_mma_cta(const Args a) {
     __syncwarp();
     const uint32_t row = lane & 15;
     const uint32_t key = key0 + min(row, valid - 1);
-    const __half *src = kv_row(a, lane >= 16, seq, key, size_t(kvh) * D);
+    const __half *src = (lane < 16 ? a.k : a.v) + seq * a.cache_stride +
+                        (size_t(key) * a.kv_heads + kvh) * D;
+    if (fresh != nullptr && key + 1 == a.keys)  // the step's new row (folded KvAppend)
+      src = fresh + seq * a.new_stride + size_t(kvh) * D;
     uint8_t *dst = stages + stage * Shape::kStageBytes + (lane < 16 ? 0 : Shape::kTileBytes) +
                    row * Shape::kRowStride;
     bulk_g2s(dst, src, Shape::kRowBytes, &bars[stage], policy);
