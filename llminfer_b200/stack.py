@@ -21,12 +21,13 @@ group r % Nh and opens an AttentionSession over that shard (B/Ns sequences,
 H/Nh of every head count; head group g of the GQA layers holds query heads
 [g Hq/Nh, (g+1) Hq/Nh) and their KV heads, of the DeltaNet layers value heads
 [g Hv/Nh, ...) and their key heads, so the kernels' head-to-group mapping is
-unchanged).  After each prefill layer the ranks all-gather that layer's head
-outputs over NCCL on a second stream, started from the layer's completion
-event (llmi_cuda_session_set_layer_events) so it overlaps the following
-layers; in decode the 32 layers' head outputs of a step are gathered by one
-collective per step.  Every all-gathered buffer is rank-major
-[N][B/Ns][T][H/Nh * D]; `unshard` turns it back into [B][T][H * D].
+unchanged).  After each prefill layer the Nh ranks of a sequence group
+all-gather that layer's head outputs over NCCL on a second stream, started
+from the layer's completion event (llmi_cuda_session_set_layer_events) so it
+overlaps the following layers; in decode the 32 layers' head outputs of a step
+are gathered by one collective per step.  A gathered buffer is rank-major
+[Nh][B/Ns][T][H/Nh * D] (of all N ranks, [N][...], when every rank's shard is
+gathered); `unshard` turns it back into [B/Ns][T][H * D] ([B][T][H * D]).
 """
 from __future__ import annotations
 
@@ -101,6 +102,21 @@ class ShardPlan:
         for h in ("query_heads", "kv_heads", "key_heads", "value_heads"):
             out[h] = shape[h] // self.head_groups
         return out
+
+
+def head_group_ranks(plan: ShardPlan, seq_group: int) -> list:
+    """The ranks holding the head shards of sequence group `seq_group`."""
+    return [seq_group * plan.head_groups + h for h in range(plan.head_groups)]
+
+
+def make_gather_group(dist, plan: ShardPlan):
+    """The process group this rank's head outputs are all-gathered in: its
+    sequence group's head shards (every rank takes part in creating each
+    group, in the same order).  None: all ranks (one sequence group)."""
+    if plan.seq_groups == 1:
+        return None
+    groups = [dist.new_group(head_group_ranks(plan, g)) for g in range(plan.seq_groups)]
+    return groups[plan.seq_group]
 
 
 def unshard(gathered, world: int, seq_groups: int, head_groups: int):
@@ -238,10 +254,16 @@ class StackRun:
         # of its sequences.
         self.gathering = dist is not None and n > 1 and plan.head_groups > 1
         self.pre_gathered = self.dec_gathered = None
+        self.group = None
         if self.gathering:
-            self.pre_gathered = torch.empty(n, self.b, prefill, self.width, dtype=torch.float16,
-                                            device=self.device)
-            self.dec_gathered = torch.empty(n, len(self.kinds), self.b, 1, self.width,
+            # Each sequence group gathers only its own head shards: a rank
+            # receives (Nh - 1) / Nh of its sequences' outputs, nothing of the
+            # other sequence groups'.
+            self.group = make_gather_group(dist, plan)
+            nh = plan.head_groups
+            self.pre_gathered = torch.empty(nh, self.b, prefill, self.width,
+                                            dtype=torch.float16, device=self.device)
+            self.dec_gathered = torch.empty(nh, len(self.kinds), self.b, 1, self.width,
                                             dtype=torch.float16, device=self.device)
 
     def _io(self, operands, outs):
@@ -261,7 +283,7 @@ class StackRun:
         # The output is passed as the ranks' inputs concatenated along dim 0,
         # the form every backend accepts; dst itself is [N][...src.shape].
         with torch.cuda.stream(self.comm):
-            self.dist.all_gather_into_tensor(dst.view(-1, *src.shape[1:]), src)
+            self.dist.all_gather_into_tensor(dst.view(-1, *src.shape[1:]), src, group=self.group)
 
     def run_prefill(self, tokens=None, operands=None):
         """Enqueues one prefill step; per-layer gathers on the comm stream."""
@@ -278,7 +300,7 @@ class StackRun:
         if self.gathering:
             for l, ev in enumerate(self.events):
                 self.comm.wait_event(ev)
-                self._gather(dense(self.pre_gathered, self.plan.world, self.b), outs[l])
+                self._gather(dense(self.pre_gathered, self.plan.head_groups, self.b), outs[l])
             self.stream.wait_stream(self.comm)
 
     def run_decode_step(self, step: int):
@@ -349,14 +371,15 @@ class StackRun:
         self.session.reset()
 
     def gathered_prefill_output(self, layer):
-        """Full [B][T][H*D] output of `layer` after a prefill (for checks)."""
+        """[B / Ns][T][H*D]: every head of `layer`'s output for this rank's
+        sequences, after a prefill (for checks)."""
         self.torch.cuda.synchronize()
         if not self.gathering:
             return self.pre_out[layer].clone()
         self._gather(self.pre_gathered, self.pre_out[layer])
         self.torch.cuda.synchronize()
-        return unshard(self.pre_gathered, self.plan.world, self.plan.seq_groups,
-                       self.plan.head_groups)
+        nh = self.plan.head_groups
+        return unshard(self.pre_gathered, nh, 1, nh)
 
     def close(self):
         self.torch.cuda.synchronize()
@@ -445,9 +468,10 @@ def run_stack(torch, dist, world, rank, batch=16, prefill=8192, decode=256, laye
                      f"{decode} decode steps"),
         "sharding": {"split": split, "sequence_groups": plan.seq_groups,
                      "head_groups": plan.head_groups,
-                     "collective": "NCCL all-gather of head outputs (prefill: per layer, "
-                                   "overlapped; decode: all layers of a step in one, inside "
-                                   "the step's CUDA graph)"
+                     "collective": f"NCCL all-gather of head outputs among the "
+                                   f"{plan.head_groups} ranks of each sequence group "
+                                   "(prefill: per layer, overlapped; decode: all layers of a "
+                                   "step in one, inside the step's CUDA graph)"
                      if world > 1 and plan.head_groups > 1 else
                      "none (whole sequences per GPU)" if world > 1 else "none (1 GPU)"},
         "prefill_ms": round(p, 3),

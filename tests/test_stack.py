@@ -137,6 +137,40 @@ def test_gloo_all_gather_reassembles_layer_output():
     assert dict(result) == {0: True, 1: True}
 
 
+def _group_gather_worker(rank, world, port, full, result):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        plan = S.ShardPlan.make(world, rank, full.shape[0], SMALL)
+        group = S.make_gather_group(dist, plan)
+        b, t, h, d = full.shape
+        mine = full[plan.seqs(b), :, plan.heads(h)].reshape(b // plan.seq_groups, t, -1)
+        nh = plan.head_groups
+        gathered = torch.empty(nh, *mine.shape, dtype=mine.dtype)
+        dist.all_gather_into_tensor(gathered.view(-1, *mine.shape[1:]), mine.contiguous(),
+                                    group=group)
+        back = S.unshard(gathered, nh, 1, nh)
+        want = full[plan.seqs(b)].reshape(b // plan.seq_groups, t, -1)
+        result[rank] = (plan.seq_groups, nh, S.head_group_ranks(plan, plan.seq_group),
+                        bool(torch.equal(back, want)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_gather_within_each_sequence_group():
+    """World 4 as 2 sequence groups x 2 head groups: each sequence group
+    gathers its own head shards (ranks {0, 1} and {2, 3}) and reassembles all
+    heads of its sequences."""
+    world = 4
+    full = torch.randn(4, 3, 8, 16)
+    result = mp.Manager().dict()
+    mp.spawn(_group_gather_worker, args=(world, _free_port(), full, result), nprocs=world,
+             join=True)
+    assert dict(result) == {0: (2, 2, [0, 1], True), 1: (2, 2, [0, 1], True),
+                            2: (2, 2, [2, 3], True), 3: (2, 2, [2, 3], True)}
+
+
 def _rank_loss_worker(rank, world, port, result):
     import datetime
     import time
