@@ -131,6 +131,30 @@ int llmi_cuda_gqa_decode_append(const llmi_gqa_params *p, unsigned batch,
                                 size_t cache_stride, uint16_t *out, void *workspace,
                                 size_t workspace_bytes, void *stream);
 
+/* Launch flag of the _ex entry points.  With it the caller guarantees that no
+ * work that may still be running when the call's kernels start writes the
+ * operands the call carries over from earlier steps: cache rows [0, past) of
+ * a decode, the recurrent state of a DeltaNet update.  That holds when the
+ * stream was synchronised after the last such write (a step-and-wait
+ * executor, as the reference's MetalExecutor.mm:255-292), or when the write
+ * belongs to an earlier CUDA graph launch on the stream.  It does not hold for
+ * two calls on the same caches or state enqueued back to back.  The
+ * decode-path kernels launch as programmatic dependents of the kernel ahead;
+ * with the flag they read those operands before that kernel has finished.
+ * The results are the same with and without it. */
+#define LLMI_FLAG_SETTLED 1u
+
+/* llmi_cuda_gqa_decode_append with launch flags (0 or LLMI_FLAG_SETTLED;
+ * other bits are LLMI_INVALID_ARGUMENT).  The same lowering
+ * (MetalExecutionPlan.cpp:516-548); the flag is the executor's knowledge of
+ * its own step order. */
+int llmi_cuda_gqa_decode_append_ex(const llmi_gqa_params *p, unsigned batch,
+                                   const uint16_t *q, const uint16_t *k_new,
+                                   const uint16_t *v_new, size_t new_stride,
+                                   uint16_t *k_cache, uint16_t *v_cache,
+                                   size_t cache_stride, uint16_t *out, void *workspace,
+                                   size_t workspace_bytes, void *stream, unsigned flags);
+
 /* Decode without a caller-provided workspace.  This entry point has no
  * counterpart in the reference.  It exists for callers that cannot allocate
  * device memory: an executor that hands out all device memory from its own
@@ -193,6 +217,16 @@ int llmi_cuda_delta_update_ws(const llmi_delta_params *p, unsigned batch,
                               const float *beta, const float *decay, float *state,
                               uint16_t *out, void *workspace, size_t workspace_bytes,
                               void *stream);
+
+/* llmi_cuda_delta_update_ws with launch flags (0 or LLMI_FLAG_SETTLED; other
+ * bits are LLMI_INVALID_ARGUMENT).  The same graphDeltaUpdate dispatch
+ * (MetalExecutionPlan.cpp:663-676); the flag affects the recurrent form
+ * (tokens < 16) only. */
+int llmi_cuda_delta_update_ws_ex(const llmi_delta_params *p, unsigned batch,
+                                 const float *q, const float *k, const uint16_t *v,
+                                 const float *beta, const float *decay, float *state,
+                                 uint16_t *out, void *workspace, size_t workspace_bytes,
+                                 void *stream, unsigned flags);
 
 /* ---- Producers of the path's operands -------------------------------------
  * The ops that turn the projections' outputs into the inputs of cacheAppend /
@@ -365,7 +399,10 @@ int llmi_cuda_session_step(llmi_session *session, unsigned tokens,
 /* Like session_step but does not wait or poll: the work is only enqueued on
  * the session stream, and past advances when the launches were accepted.
  * For timed loops and CUDA-graph capture; follow with
- * llmi_cuda_session_sync before trusting the results. */
+ * llmi_cuda_session_sync before trusting the results.  A step enqueued right
+ * after a synchronised one, or as the first step of a stream capture, passes
+ * LLMI_FLAG_SETTLED to its decode-path calls; one enqueued behind an
+ * unsynchronised step does not. */
 int llmi_cuda_session_enqueue(llmi_session *session, unsigned tokens,
                               const llmi_layer_io *io);
 /* Waits for the session stream and checks the device error word; on failure
@@ -394,7 +431,11 @@ uint64_t llmi_cuda_session_past(const llmi_session *session);
 int llmi_cuda_session_is_invalid(const llmi_session *session);
 
 /* Device pointer and size of one state buffer of `layer`
- * (which = LLMI_STATE_*). */
+ * (which = LLMI_STATE_*).  Work that writes a buffer through this pointer
+ * must be complete before the session's next step is issued (e.g. followed
+ * by a stream synchronisation): after a synchronised step, and for the first
+ * step of a stream capture, the session's decode-path calls pass
+ * LLMI_FLAG_SETTLED. */
 int llmi_cuda_session_state(llmi_session *session, unsigned layer,
                             unsigned which, void **pointer, size_t *bytes);
 

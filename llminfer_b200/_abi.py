@@ -22,6 +22,8 @@ LLMI_WORKSPACE_TOO_SMALL = 5
 LLMI_SESSION_INVALID = 6
 LLMI_CAPACITY_EXCEEDED = 7
 
+LLMI_FLAG_SETTLED = 1  # launch flag of the _ex entry points (include/llmi_cuda.h)
+
 LAYER_DELTANET = 0
 LAYER_GQA = 1
 
@@ -116,6 +118,9 @@ SIGNATURES = [
     ("llmi_cuda_gqa_decode_append", c_int,
      [POINTER(GqaParams), c_uint, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p,
       c_size_t, c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("llmi_cuda_gqa_decode_append_ex", c_int,
+     [POINTER(GqaParams), c_uint, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p,
+      c_size_t, c_void_p, c_void_p, c_size_t, c_void_p, c_uint]),
     ("llmi_cuda_gqa_decode_noalloc", c_int,
      [POINTER(GqaParams), c_uint, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     ("llmi_cuda_delta_update", c_int,
@@ -125,6 +130,9 @@ SIGNATURES = [
     ("llmi_cuda_delta_update_ws", c_int,
      [POINTER(DeltaParams), c_uint, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
       c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("llmi_cuda_delta_update_ws_ex", c_int,
+     [POINTER(DeltaParams), c_uint, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+      c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_uint]),
     ("llmi_cuda_norm_rope", c_int,
      [POINTER(RopeParams), c_uint, c_void_p, c_size_t, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("llmi_cuda_partial_rope", c_int,

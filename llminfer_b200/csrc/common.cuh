@@ -42,6 +42,11 @@ __device__ __forceinline__ void raise_error(unsigned bits) { atomicOr(&g_error_w
 // overlap this one's tail, and
 // since every kernel waits for its predecessor before finishing, the chain
 // stays ordered.  Without the launch attribute both are no-ops.
+// The one exception is a call flagged `settled` by its caller (the session
+// between synchronised or separately launched steps): the operands it only
+// carries over from earlier steps (cache rows before the newest, the
+// recurrent state) are then known complete, and the kernel reads them before
+// its wait, while the kernel ahead still runs.
 __device__ __forceinline__ void launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }

@@ -27,6 +27,10 @@ struct Args {
   float *state;            // [batch][Hv][dk][dv]
   __half *out;             // [batch][tokens][Hv*dv]
   uint32_t batch, tokens, key_heads, key_dim, value_heads, value_dim, group;
+  // Nonzero when the caller guarantees that no work still in flight writes
+  // the state (LLMI_FLAG_SETTLED): recurrent_v32 then loads it into
+  // registers before wait_primary(), while the kernel ahead still runs.
+  uint32_t settled;
 };
 
 constexpr int kRecWarps = 8;
@@ -148,18 +152,25 @@ __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v32(const Args a) {
   const uint32_t seq = blockIdx.y, kh = vh / a.group;
   const uint32_t col = blk * kCols + 4 * cg;  // this lane's first column within the head
   float *S = a.state + (size_t(seq) * a.value_heads + vh) * DK * DV;
-  // This block's state into L2 while the kernel ahead still runs (a prefetch
-  // never changes what a later load returns): one 128-byte row segment per
-  // thread.
-  if (threadIdx.x < DK)
-    prefetch_l2(S + size_t(threadIdx.x) * DV + blk * kCols, kCols * 4);
-  pdl_enter();
+  // A settled state is loaded into registers before the wait.  Otherwise
+  // this block's state goes into L2 while the kernel ahead still runs (a
+  // prefetch never changes what a later load returns; one 128-byte row
+  // segment per thread) and is loaded after the wait.
   auto row_of = [&](int p) { return warp * 4 + rs + 32 * p; };
-
   float4 s[R];
+  if (a.settled) {
 #pragma unroll
-  for (int p = 0; p < R; ++p)
-    s[p] = ld_stream_f4(S + size_t(row_of(p)) * DV + col);
+    for (int p = 0; p < R; ++p)
+      s[p] = ld_stream_f4(S + size_t(row_of(p)) * DV + col);
+    pdl_enter();
+  } else {
+    if (threadIdx.x < DK)
+      prefetch_l2(S + size_t(threadIdx.x) * DV + blk * kCols, kCols * 4);
+    pdl_enter();
+#pragma unroll
+    for (int p = 0; p < R; ++p)
+      s[p] = ld_stream_f4(S + size_t(row_of(p)) * DV + col);
+  }
 
   const size_t key_width = size_t(a.key_heads) * DK;
   const size_t value_width = size_t(a.value_heads) * DV;

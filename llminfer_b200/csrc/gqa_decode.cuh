@@ -96,6 +96,10 @@ struct Args {
   const __half *k_new, *v_new;
   size_t new_stride;
   uint32_t batch;
+  // Nonzero when the caller guarantees that no work still in flight writes
+  // cache rows [0, keys - 1) (LLMI_FLAG_SETTLED): partial_rows then requests
+  // its first tiles below the newest row before wait_primary().
+  uint32_t settled;
 };
 
 // L2 warm-up of a CTA worker's first key tiles, issued before
@@ -260,9 +264,10 @@ __global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
   const uint32_t total = pt.units * pt.tiles_per_unit;
   const uint32_t begin = min(total, worker * pt.tiles_per_worker);
   const uint32_t end = min(total, begin + pt.tiles_per_worker);
-  pdl_enter();  // before the first global read
-  if (begin >= end)
+  if (begin >= end) {
+    pdl_enter();
     return;  // uniform over the CTA
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -286,9 +291,19 @@ __global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
     // Tile t is keys [key0, key0 + 16) of sequence seq; both advance with t
     // (no division per tile: the copies' issue is on the pipeline's path).
     uint32_t seq = begin / tpu, key0 = (begin % tpu) * kTileKeys;
+    // Settled caches: the first STAGES tiles that end below the newest row
+    // are requested before the wait (the newest row may come from the kernel
+    // ahead: `fresh`, or a separate cacheAppend).
+    bool waited = !a.settled;
+    if (waited)
+      pdl_enter();
     for (uint32_t t = begin; t < end; ++t) {
       const uint32_t j = t - begin;
       const int s = j % STAGES;
+      if (!waited && (j >= STAGES || key0 + kTileKeys >= a.keys)) {
+        pdl_enter();
+        waited = true;
+      }
       if (j >= STAGES &&
           !__all_sync(0xffffffffu, wait_or_abort(&empty[s], ((j / STAGES) - 1) & 1, abort)))
         break;
@@ -311,6 +326,8 @@ __global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
         ++seq;
       }
     }
+    if (!waited)
+      pdl_enter();
     // Every issued copy lands before the CTA can exit (bounded).
     if (lane == 0)
       for (uint32_t j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
@@ -319,6 +336,7 @@ __global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
     return;
   }
 
+  pdl_enter();  // before the queries are read
   // Consumer warp: kv head `warp`.
   const uint32_t h = warp;
   TileMath<D> math;

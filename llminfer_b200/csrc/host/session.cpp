@@ -39,6 +39,14 @@ struct llmi_session {
   size_t workspaceBytes = 0;
   uint64_t past = 0;
   bool invalid = false;
+  // Whether this session's earlier steps are complete before the next step's
+  // kernels can start, so that its decode-path calls may pass
+  // LLMI_FLAG_SETTLED for the caches and states they carry over: yes after a
+  // synchronising step or sync; no after an eagerly enqueued step; under
+  // stream capture, yes for the first step of a capture (a graph launch runs
+  // after all earlier work on its stream), no for later ones.
+  bool inFlight = false;
+  unsigned long long lastCaptureId = 0;
   std::string plan;
   std::vector<cudaEvent_t> layerEvents;  // borrowed; recorded after each layer
   unsigned injectFaultUs = 0;             // > 0: the next step also runs the wait self-test
@@ -176,6 +184,30 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
   AttentionGraph graph;
   if (int e = AttentionGraph::build(s.config, {tokens, s.past, s.config.capacity}, graph))
     return e;
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  unsigned long long captureId = 0;
+  if (int e = check_cuda(cudaStreamGetCaptureInfo(s.stream, &capture, &captureId),
+                         "cudaStreamGetCaptureInfo"))
+    return e;
+  const bool capturing = capture == cudaStreamCaptureStatusActive;
+  // Each layer's caches and state are written once per step, by its own op,
+  // so within a step nothing ahead of an op writes what it carries over.
+  const unsigned flags =
+      (capturing ? captureId != s.lastCaptureId : !s.inFlight) ? LLMI_FLAG_SETTLED : 0u;
+  struct Mark {
+    llmi_session &s;
+    bool capturing;
+    unsigned long long id;
+    const bool &launched;
+    ~Mark() {
+      if (!launched)
+        return;
+      if (capturing)
+        s.lastCaptureId = id;
+      else
+        s.inFlight = true;
+    }
+  } mark{s, capturing, captureId, launchedAny};
   const StackConfig &c = s.config;
   const unsigned B = c.batch;
   std::vector<llmi_layer_io> produced;
@@ -331,11 +363,11 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
                                   static_cast<const uint16_t *>(s.values[op.layer]), cacheStride,
                                   static_cast<uint16_t *>(x.out), s.stream);
       } else if (foldK || foldV) {
-        e = llmi_cuda_gqa_decode_append(
+        e = llmi_cuda_gqa_decode_append_ex(
             &p, B, static_cast<const uint16_t *>(x.q), foldK, foldV,
             size_t(c.kvHeads) * c.headDim, static_cast<uint16_t *>(s.keys[op.layer]),
             static_cast<uint16_t *>(s.values[op.layer]), cacheStride,
-            static_cast<uint16_t *>(x.out), s.workspace, s.workspaceBytes, s.stream);
+            static_cast<uint16_t *>(x.out), s.workspace, s.workspaceBytes, s.stream, flags);
         foldK = foldV = nullptr;
         count = 2;
       } else {
@@ -351,12 +383,12 @@ int run_step(llmi_session &s, unsigned tokens, const llmi_layer_io *io, bool tra
     case OpKind::DeltaUpdate: {
       llmi_delta_params p{tokens, c.keyHeads, c.keyDim, c.valueHeads, c.valueDim};
       launchedAny = true;
-      e = llmi_cuda_delta_update_ws(&p, B, static_cast<const float *>(x.q),
-                                    static_cast<const float *>(x.k),
-                                    static_cast<const uint16_t *>(x.v), x.beta, x.decay,
-                                    static_cast<float *>(s.recurrent[op.layer]),
-                                    static_cast<uint16_t *>(x.out), s.workspace,
-                                    s.workspaceBytes, s.stream);
+      e = llmi_cuda_delta_update_ws_ex(&p, B, static_cast<const float *>(x.q),
+                                       static_cast<const float *>(x.k),
+                                       static_cast<const uint16_t *>(x.v), x.beta, x.decay,
+                                       static_cast<float *>(s.recurrent[op.layer]),
+                                       static_cast<uint16_t *>(x.out), s.workspace,
+                                       s.workspaceBytes, s.stream, flags);
       break;
     }
     }
@@ -478,6 +510,7 @@ int step_and_wait(llmi_session *s, unsigned tokens, const llmi_layer_io *io,
     s->invalid = launchedAny;
     return e;
   }
+  s->inFlight = false;  // poll_error synchronised the stream
   s->past += tokens;
   return LLMI_OK;
 }
@@ -560,6 +593,7 @@ extern "C" int llmi_cuda_session_sync(llmi_session *s) {
     s->invalid = true;
     return e;
   }
+  s->inFlight = false;
   return LLMI_OK;
 }
 
@@ -601,6 +635,7 @@ extern "C" int llmi_cuda_session_reset(llmi_session *s) {
     return fail(LLMI_INVALID_ARGUMENT, "reset: null session");
   if (int e = zero_states(*s))
     return e;
+  s->inFlight = false;  // zero_states synchronised the stream
   s->past = 0;
   s->invalid = false;
   s->plan.clear();

@@ -629,7 +629,7 @@ struct NewRows {
 int gqa_decode_run(const llmi_gqa_params *p, unsigned batch, const uint16_t *q,
                    const uint16_t *k_cache, const uint16_t *v_cache, size_t cache_stride,
                    uint16_t *out, void *workspace, size_t workspace_bytes, void *stream,
-                   NewRows fresh) {
+                   NewRows fresh, unsigned flags = 0) {
   if (!workspace)
     return fail(LLMI_INVALID_ARGUMENT, "decode: null workspace");
   DeviceInfo dev;
@@ -681,6 +681,7 @@ int gqa_decode_run(const llmi_gqa_params *p, unsigned batch, const uint16_t *q,
   a.v_new = reinterpret_cast<const __half *>(fresh.v);
   a.new_stride = fresh.stride;
   a.batch = batch;
+  a.settled = (flags & LLMI_FLAG_SETTLED) ? 1u : 0u;
   cudaStream_t s = as_stream(stream);
   int status = LLMI_OK;
   switch (plan.kind) {
@@ -744,7 +745,20 @@ extern "C" int llmi_cuda_gqa_decode_append(const llmi_gqa_params *p, unsigned ba
                                            uint16_t *k_cache, uint16_t *v_cache,
                                            size_t cache_stride, uint16_t *out, void *workspace,
                                            size_t workspace_bytes, void *stream) {
+  return llmi_cuda_gqa_decode_append_ex(p, batch, q, k_new, v_new, new_stride, k_cache, v_cache,
+                                        cache_stride, out, workspace, workspace_bytes, stream, 0u);
+}
+
+extern "C" int llmi_cuda_gqa_decode_append_ex(const llmi_gqa_params *p, unsigned batch,
+                                              const uint16_t *q, const uint16_t *k_new,
+                                              const uint16_t *v_new, size_t new_stride,
+                                              uint16_t *k_cache, uint16_t *v_cache,
+                                              size_t cache_stride, uint16_t *out,
+                                              void *workspace, size_t workspace_bytes,
+                                              void *stream, unsigned flags) {
   clear_error();
+  if (flags & ~LLMI_FLAG_SETTLED)
+    return fail(LLMI_INVALID_ARGUMENT, "decode_append: unknown flags 0x%x", flags);
   if (int s = check_gqa(p, batch, q, k_cache, v_cache, cache_stride, out))
     return s;
   if (p->tokens != 1)
@@ -756,7 +770,7 @@ extern "C" int llmi_cuda_gqa_decode_append(const llmi_gqa_params *p, unsigned ba
   if (batch > 1 && (k_new || v_new) && new_stride < row)
     return fail(LLMI_INVALID_ARGUMENT, "decode_append: new rows of sequences overlap");
   return gqa_decode_run(p, batch, q, k_cache, v_cache, cache_stride, out, workspace,
-                        workspace_bytes, stream, NewRows{k_new, v_new, new_stride});
+                        workspace_bytes, stream, NewRows{k_new, v_new, new_stride}, flags);
 }
 
 // ---- decode without a caller workspace ------------------------------------------------
@@ -856,7 +870,7 @@ size_t delta_solved_bytes(const llmi_delta_params *p, unsigned batch) {
 int delta_update_impl(const llmi_delta_params *p, unsigned batch, const float *q, const float *k,
                       const uint16_t *v, const float *beta, const float *decay, float *state,
                       uint16_t *out, void *workspace, size_t workspace_bytes, bool with_ws,
-                      void *stream);
+                      void *stream, unsigned flags = 0);
 
 }  // namespace
 
@@ -888,12 +902,26 @@ extern "C" int llmi_cuda_delta_update_ws(const llmi_delta_params *p, unsigned ba
                            workspace_bytes, true, stream);
 }
 
+extern "C" int llmi_cuda_delta_update_ws_ex(const llmi_delta_params *p, unsigned batch,
+                                            const float *q, const float *k, const uint16_t *v,
+                                            const float *beta, const float *decay, float *state,
+                                            uint16_t *out, void *workspace,
+                                            size_t workspace_bytes, void *stream,
+                                            unsigned flags) {
+  if (flags & ~LLMI_FLAG_SETTLED) {
+    clear_error();
+    return fail(LLMI_INVALID_ARGUMENT, "DeltaUpdate: unknown flags 0x%x", flags);
+  }
+  return delta_update_impl(p, batch, q, k, v, beta, decay, state, out, workspace,
+                           workspace_bytes, true, stream, flags);
+}
+
 namespace {
 
 int delta_update_impl(const llmi_delta_params *p, unsigned batch, const float *q, const float *k,
                       const uint16_t *v, const float *beta, const float *decay, float *state,
                       uint16_t *out, void *workspace, size_t workspace_bytes, bool with_ws,
-                      void *stream) {
+                      void *stream, unsigned flags) {
   clear_error();
   if (!p || !q || !k || !v || !beta || !decay || !state || !out)
     return fail(LLMI_INVALID_ARGUMENT, "DeltaUpdate: null parameter or tensor pointer");
@@ -917,6 +945,7 @@ int delta_update_impl(const llmi_delta_params *p, unsigned batch, const float *q
   a.value_heads = p->valueHeads;
   a.value_dim = p->valueDim;
   a.group = p->valueHeads / p->keyHeads;
+  a.settled = (flags & LLMI_FLAG_SETTLED) ? 1u : 0u;
   cudaStream_t s = as_stream(stream);
   // Multi-token calls: chunked form on tensor cores (dk = dv = 128).
   const bool chunked = delta_chunked(p, batch, q, k, v, state, out);

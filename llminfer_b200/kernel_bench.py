@@ -397,7 +397,8 @@ def bench_step(args):
     into a CUDA graph and replayed (device time per replay): 8 GQA layers (KvAppend
     + decode, through llmi_cuda_gqa_decode_append as the session issues them, and
     as three separate calls) and 24 recurrent DeltaNet layers, interleaved as in
-    the hybrid stack (three DeltaNet layers, then one GQA layer)."""
+    the hybrid stack (three DeltaNet layers, then one GQA layer).  The step
+    is timed with and without LLMI_FLAG_SETTLED on its decode-path calls."""
     g = torch.Generator(device="cuda").manual_seed(args.seed)
     B, (Hq, Hkv), D, P, cap = args.batch, args.heads, args.dim, args.past, args.capacity
     (Hk, Hv), (dk, dv) = args.delta_heads, args.delta_dims
@@ -420,16 +421,24 @@ def bench_step(args):
               for _ in range(dlayers)]
     dout = torch.empty_like(dvv)
 
+    dws = torch.empty(16, dtype=torch.uint8, device="cuda")  # T = 1 takes no scratch
+    # Settled launches (LLMI_FLAG_SETTLED), as the session issues them: every
+    # layer has its own caches and state, each appears once per captured
+    # graph, and graph replays run one after another.
+    settled = [True]
+
     def gqa(l, folded=True):
         if folded:
-            ops.gqa_decode_append(q, kn, vn, kc[l], vc[l], P, out=out, workspace=ws)
+            ops.gqa_decode_append(q, kn, vn, kc[l], vc[l], P, out=out, workspace=ws,
+                                  settled=settled[0])
         else:
             ops.cache_append(kn, kc[l], P)
             ops.cache_append(vn, vc[l], P)
             ops.gqa_decode(q, kc[l], vc[l], P, out=out, workspace=ws)
 
     def rec(l):
-        ops.delta_update(dq, dkk, dvv, beta, decay, states[l], out=dout, workspace=False)
+        ops.delta_update(dq, dkk, dvv, beta, decay, states[l], out=dout, workspace=dws,
+                         settled=settled[0])
 
     def step(folded=True):
         for i in range(layers):
@@ -437,12 +446,22 @@ def bench_step(args):
                 rec(3 * i + j)
             gqa(i, folded)
 
+    def unsettled(fn):
+        def run():
+            settled[0] = False
+            try:
+                fn()
+            finally:
+                settled[0] = True
+        return run
+
     reps = max(args.samples, 5)
     us = lambda fn, n=1: round(time_graph(fn, reps) * 1000 / n, 2)
     return {"op": "decode step", "batch": B, "heads": [Hq, Hkv], "dim": D, "past": P,
             "capacity": cap, "gqa_layers": layers, "delta_layers": dlayers,
             "delta_heads": [Hk, Hv], "delta_dims": [dk, dv],
-            "us_step": us(step), "us_step_separate_appends": us(lambda: step(False)),
+            "us_step": us(step), "us_step_unsettled": us(unsettled(step)),
+            "us_step_separate_appends": us(lambda: step(False)),
             "us_gqa_layer": us(lambda: [gqa(l) for l in range(layers)], layers),
             "us_gqa_layer_separate_appends":
                 us(lambda: [gqa(l, False) for l in range(layers)], layers),

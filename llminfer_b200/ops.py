@@ -102,10 +102,17 @@ def gqa_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pa
 def gqa_decode_append(q: torch.Tensor, k_new: torch.Tensor | None, v_new: torch.Tensor | None,
                       k_cache: torch.Tensor, v_cache: torch.Tensor, past: int,
                       out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
-                      stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+                      stream: torch.cuda.Stream | None = None,
+                      settled: bool = False) -> torch.Tensor:
     """KvAppend + decode in one pass: writes k_new / v_new [B, 1, Hkv, D] (None: that
     row is already in the cache) into cache row `past`, then decodes over rows
-    [0, past] like gqa_decode."""
+    [0, past] like gqa_decode.
+
+    settled=True passes LLMI_FLAG_SETTLED: the caller guarantees that no work
+    still running when the call starts writes cache rows [0, past) (the stream
+    was synchronised after the last write, or the write belongs to an earlier
+    CUDA graph launch).  Same results; the kernels read those rows before the
+    kernel ahead has finished."""
     for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
         _need(t, torch.float16, n)
     p = _gqa_params(q, k_cache, past)
@@ -127,12 +134,13 @@ def gqa_decode_append(q: torch.Tensor, k_new: torch.Tensor | None, v_new: torch.
         workspace = torch.empty(n, dtype=torch.uint8, device=q.device)
     out = torch.empty_like(q) if out is None else out
     _need(out, torch.float16, "out")
-    check(lib.llmi_cuda_gqa_decode_append(
+    check(lib.llmi_cuda_gqa_decode_append_ex(
         ctypes.byref(p), q.shape[0], q.data_ptr(),
         k_new.data_ptr() if k_new is not None else None,
         v_new.data_ptr() if v_new is not None else None, new_stride or row,
         k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0), out.data_ptr(),
-        workspace.data_ptr(), workspace.numel(), _stream(stream)))
+        workspace.data_ptr(), workspace.numel(), _stream(stream),
+        abi.LLMI_FLAG_SETTLED if settled else 0))
     return out
 
 
@@ -146,13 +154,16 @@ def delta_workspace_bytes(batch: int, tokens: int, key_heads: int, key_dim: int,
 def delta_update(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
                  decay: torch.Tensor, state: torch.Tensor, out: torch.Tensor | None = None,
                  workspace: torch.Tensor | bool | None = None,
-                 stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+                 stream: torch.cuda.Stream | None = None,
+                 settled: bool = False) -> torch.Tensor:
     """graphDeltaUpdate: updates state [B, Hv, dk, dv] in place, returns out [B, T, Hv*dv].
 
     workspace None allocates the scratch of the chunk-parallel form
     (llmi_cuda_delta_update_ws); a uint8 tensor is used as that scratch;
     False calls llmi_cuda_delta_update, which takes no scratch (one kernel
-    walks each head's chunks and solves their systems in order)."""
+    walks each head's chunks and solves their systems in order).
+    settled=True (not with workspace=False) passes LLMI_FLAG_SETTLED, with the
+    guarantee gqa_decode_append states, for the state."""
     for t, n in ((q, "q"), (k, "k"), (beta, "beta"), (decay, "decay"), (state, "state")):
         _need(t, torch.float32, n)
     _need(v, torch.float16, "v")
@@ -162,6 +173,8 @@ def delta_update(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.
     out = torch.empty_like(v) if out is None else out
     _need(out, torch.float16, "out")
     if workspace is False:
+        if settled:
+            raise ValueError("delta_update: settled needs the workspace entry point")
         check(lib.llmi_cuda_delta_update(ctypes.byref(p), B, q.data_ptr(), k.data_ptr(),
                                          v.data_ptr(), beta.data_ptr(), decay.data_ptr(),
                                          state.data_ptr(), out.data_ptr(), _stream(stream)))
@@ -169,10 +182,12 @@ def delta_update(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.
     if workspace is None:
         n = lib.llmi_cuda_delta_update_workspace(ctypes.byref(p), B)
         workspace = torch.empty(max(n, 16), dtype=torch.uint8, device=q.device)
-    check(lib.llmi_cuda_delta_update_ws(ctypes.byref(p), B, q.data_ptr(), k.data_ptr(),
-                                        v.data_ptr(), beta.data_ptr(), decay.data_ptr(),
-                                        state.data_ptr(), out.data_ptr(), workspace.data_ptr(),
-                                        workspace.numel(), _stream(stream)))
+    check(lib.llmi_cuda_delta_update_ws_ex(ctypes.byref(p), B, q.data_ptr(), k.data_ptr(),
+                                           v.data_ptr(), beta.data_ptr(), decay.data_ptr(),
+                                           state.data_ptr(), out.data_ptr(),
+                                           workspace.data_ptr(), workspace.numel(),
+                                           _stream(stream),
+                                           abi.LLMI_FLAG_SETTLED if settled else 0))
     return out
 
 

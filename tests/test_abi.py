@@ -154,3 +154,18 @@ def test_argument_errors_precede_any_device_use():
     c = abi.CacheParams(8, 0)
     assert lib.llmi_cuda_cache_append(ctypes.byref(c), 0, one, 8, one, 8, None) == abi.LLMI_INVALID_ARGUMENT
     assert "null" in lib.llmi_cuda_last_error().decode() or "zero" in lib.llmi_cuda_last_error().decode()
+
+
+def test_unknown_launch_flags_are_rejected_before_any_device_use():
+    lib = abi.lib
+    one = ctypes.c_void_p(16)
+    g = abi.GqaParams(1, 16, 4, 256, 7)
+    status = lib.llmi_cuda_gqa_decode_append_ex(ctypes.byref(g), 1, one, one, one, 1024, one, one,
+                                                1 << 20, one, one, 1 << 20, None, 2)
+    assert status == abi.LLMI_INVALID_ARGUMENT
+    assert "flags" in lib.llmi_cuda_last_error().decode()
+    d = abi.DeltaParams(1, 16, 128, 32, 128)
+    status = lib.llmi_cuda_delta_update_ws_ex(ctypes.byref(d), 1, one, one, one, one, one, one,
+                                              one, one, 16, None, abi.LLMI_FLAG_SETTLED | 4)
+    assert status == abi.LLMI_INVALID_ARGUMENT
+    assert "flags" in lib.llmi_cuda_last_error().decode()

@@ -95,6 +95,39 @@ def test_presolved_rejects_small_workspace():
     assert torch.isnan(out).all()
 
 
+@pytest.mark.parametrize("batch,tokens,hk,dk", [
+    (2, 1, 16, 128),    # a sequence-major 8-GPU rank's step: 32-column CTAs
+    (16, 1, 16, 128),   # the 1-GPU stack's step
+    (3, 5, 16, 128),    # a few tokens
+    (8, 2, 8, 64),      # dk 64
+    (20, 1, 16, 128),   # 128-column CTAs (the flag does not change them)
+])
+def test_settled_update_matches_unsettled(batch, tokens, hk, dk):
+    """llmi_cuda_delta_update_ws_ex with LLMI_FLAG_SETTLED: the state is loaded
+    before the kernel ahead finishes.  Three layers' states back to back, as a
+    session step issues them, after a synchronisation: the same output and
+    state bits as the calls without the flag."""
+    cases = [_inputs.delta_case(batch, tokens, hk, dk, 32, 128, state_std=0.02, seed=70 + l)
+             for l in range(3)]
+    ws = torch.empty(16, dtype=torch.uint8, device="cuda")
+    results = {}
+    for settled in (False, True):
+        states = [dev(c["state"]) for c in cases]
+        outs = [torch.full(c["v"].shape, float("nan"), dtype=torch.float16, device="cuda")
+                for c in cases]
+        args = [[dev(c[n]) for n in ("q", "k", "v", "beta", "decay")] for c in cases]
+        torch.cuda.synchronize()
+        for a, st, out in zip(args, states, outs):
+            ops.delta_update(*a, st, out=out, workspace=ws, settled=settled)
+        torch.cuda.synchronize()
+        results[settled] = (outs, states)
+    for a, b in zip(results[False][0], results[True][0]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    for a, b in zip(results[False][1], results[True][1]):
+        assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+    check(cases[0], results[True][0][0].float().cpu().numpy(), results[True][1][0].cpu().numpy())
+
+
 @pytest.mark.parametrize("form", sorted(FORMS))
 def test_delta_matches_transformers_fixture(form):
     d = np.load(GOLDEN / "delta_xcheck.npz")

@@ -161,6 +161,45 @@ def test_decode_append_matches_separate_calls(batch, past, hq, hkv, d, keys_give
     assert torch.equal(vc_b.view(torch.int16), vc_a.view(torch.int16))
 
 
+@pytest.mark.parametrize("batch,past,hq,hkv,d", [
+    (2, 8320, 16, 4, 256),   # a sequence-major 8-GPU rank's decode (whole 2 KiB rows)
+    (3, 700, 16, 4, 256),
+    (2, 515, 8, 2, 256),
+    (2, 333, 16, 8, 128),
+    (8, 2000, 4, 1, 256),    # CTA workers (the flag does not change this pass)
+    (2, 20, 16, 4, 256),     # every worker's first tile holds the newest row
+    (1, 0, 16, 4, 256),      # the newest row is the only key
+])
+def test_settled_decode_matches_unsettled(batch, past, hq, hkv, d):
+    """llmi_cuda_gqa_decode_append_ex with LLMI_FLAG_SETTLED: cache rows [0, past)
+    are requested before the kernel ahead finishes.  Two layers back to back, as
+    a session step issues them, after a synchronisation (what the flag asks
+    for): the same output bits and caches as the calls without the flag."""
+    layers = []
+    for l in range(2):
+        q, k, v = _inputs.gqa_case(batch, 1, past, hq, hkv, d, capacity=past + 3,
+                                   seed=60 + past + l)
+        kn = dev(_inputs.half_normal(1, 61 + l, (batch, 1, hkv, d)))
+        vn = dev(_inputs.half_normal(1, 63 + l, (batch, 1, hkv, d)))
+        layers.append((dev(q), kn, vn, dev(k), dev(v)))
+    results = {}
+    for settled in (False, True):
+        caches = [(kc.clone(), vc.clone()) for _, _, _, kc, vc in layers]
+        outs = [nan_like(q) for q, *_ in layers]
+        torch.cuda.synchronize()
+        for (q, kn, vn, _, _), (kc, vc), out in zip(layers, caches, outs):
+            ops.gqa_decode_append(q, kn, vn, kc, vc, past, out=out, settled=settled)
+        torch.cuda.synchronize()
+        results[settled] = (outs, caches)
+    for a, b in zip(results[False][0], results[True][0]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    for (ka, va), (kb, vb) in zip(results[False][1], results[True][1]):
+        assert torch.equal(ka.view(torch.int16), kb.view(torch.int16))
+        assert torch.equal(va.view(torch.int16), vb.view(torch.int16))
+    check_bar(results[True][0][0], _oracle.gqa_dense(*(t.cpu().numpy() for t in (
+        layers[0][0], results[True][1][0][0], results[True][1][0][1])), past))
+
+
 def test_decode_rejects_small_workspace():
     q, k, v = _inputs.gqa_case(2, 1, 100, 16, 4, 256, seed=13)
     small = torch.empty(256, dtype=torch.uint8, device="cuda")
