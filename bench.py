@@ -3,7 +3,8 @@
 
 Headline workload ("C2"): one GQA decode step per
 sequence - cacheAppend of the new key/value rows, then split-K decode
-attention (gqaScores + gqaSoftmax) over past 4096 cached tokens - for a batch
+attention (gqaScores + gqaSoftmax) over past 4096 cached tokens, with the
+appends folded into the decode's two kernels as the session lowers them - for a batch
 of 64 sequences per GPU, Hq 16 / Hkv 4 / head_dim 256, fp16 caches of
 capacity 8192.  The metric is HBM throughput: the logical bytes of the
 step's ops under the reference cost model (lib/GraphIR/Cost.cpp:85-93) per
@@ -396,10 +397,11 @@ def run_ours(args, dist):
                                                 C2["head_dim"], P), dtype=torch.uint8,
                      device=device)
 
+    # A decode step as the session lowers it: the KvAppend pair folded into
+    # the decode's two kernels (llmi_cuda_gqa_decode_append).  Steps are
+    # enqueued back to back on the same caches, so no settled flag.
     def step():
-        ops.cache_append(kn, kc, P)
-        ops.cache_append(vn, vc, P)
-        ops.gqa_decode(q, kc, vc, P, out=out, workspace=ws)
+        ops.gqa_decode_append(q, kn, vn, kc, vc, P, out=out, workspace=ws)
 
     costs = step_bytes([1], 1, P, C2["capacity"], C2["batch"], query_heads=C2["query_heads"],
                        kv_heads=C2["kv_heads"], head_dim=C2["head_dim"])
@@ -419,9 +421,7 @@ def run_ours(args, dist):
     with ClockSampler(torch, device) as clocks:
         start.record()
         for i in range(K):
-            ops.cache_append(kn, kc, P)
-            ops.cache_append(vn, vc, P)
-            ops.gqa_decode(q, kc, vc, P, out=out, workspace=ws)
+            step()
         end.record()
         torch.cuda.synchronize()
     dist.barrier()
@@ -476,9 +476,7 @@ def run_ours(args, dist):
             uploaded[b].record(up)
         compute.wait_event(uploaded[b])
         compute.wait_event(read_back[b])  # step i - 2's output has left dout[b]
-        ops.cache_append(dk[b], kc, P)
-        ops.cache_append(dv[b], vc, P)
-        ops.gqa_decode(dq[b], kc, vc, P, out=dout[b], workspace=ws)
+        ops.gqa_decode_append(dq[b], dk[b], dv[b], kc, vc, P, out=dout[b], workspace=ws)
         consumed[b].record(compute)
         with torch.cuda.stream(down):
             down.wait_event(consumed[b])
@@ -573,7 +571,7 @@ def run_ours(args, dist):
                 "ms_per_step": round(e2e_ms / K, 4),
                 "copies": "pinned host buffers; uploads and read-backs on their own streams, "
                           "double-buffered, overlapping the neighbouring steps' kernels"},
-        "gpu_launches": 4 * K,
+        "gpu_launches": 2 * K,
         "clocks": clocks.summary(),
         "secondary": secondary,
         "stack": stack,
@@ -728,14 +726,16 @@ def run_strong(torch, ops, device, peaks, dist, g):
         ws = torch.empty(ops.decode_workspace_bytes(B, Hq, Hkv, D, P), dtype=torch.uint8,
                          device=device)
 
+        # KvAppend folded into the decode, with settled cache rows, as the
+        # session issues a decode step: every replay is its own graph launch,
+        # so the rows [0, P) it reads are complete before it starts.
         def fn():
-            ops.cache_append(kn, kc, P)
-            ops.cache_append(kn, vc, P)
-            ops.gqa_decode(q, kc, vc, P, out=o, workspace=ws)
+            ops.gqa_decode_append(q, kn, kn, kc, vc, P, out=o, workspace=ws, settled=True)
         return fn, seq_bytes * B
 
     out.append(line("C2 GQA decode step, 64 sequences in all (cacheAppend x2 + gqaScores + "
-                    "gqaSoftmax)", f"{64 // N} sequences per GPU", make_c2, seq_bytes * 64))
+                    "gqaSoftmax, the appends folded into the decode's kernels)",
+                    f"{64 // N} sequences per GPU", make_c2, seq_bytes * 64))
 
     # C3: DeltaNet prefill, B=4, T=4096, 128 (sequence, value head) units.
     B3, T3 = 4, 4096
@@ -764,7 +764,10 @@ def run_strong(torch, ops, device, peaks, dist, g):
         B = 256 if whole else 256 // N
         q, k, v, beta, decay, state = delta_inputs(torch, device, g, B, 1, 16, 32, 0.02)
         o = torch.empty_like(v)
-        return (lambda: ops.delta_update(q, k, v, beta, decay, state, out=o, workspace=False)), 0
+        ws = torch.empty(16, dtype=torch.uint8, device=device)  # one token takes no scratch
+        # Settled state: each replay is its own graph launch.
+        return (lambda: ops.delta_update(q, k, v, beta, decay, state, out=o, workspace=ws,
+                                         settled=True)), 0
 
     out.append(line("C4 DeltaNet recurrent step, 256 sequences in all (graphDeltaUpdate)",
                     f"{256 // N} sequences per GPU", make_c4, cost4[0]))
