@@ -34,6 +34,13 @@ struct Args {
 };
 
 constexpr int kRecWarps = 8;
+// recurrent_v32 comes in two register budgets.  A grid that fits on the GPU
+// in one wave (B = 2: 256 CTAs) takes the unbounded form, whose address
+// arithmetic stays ahead of the wait (56 registers, four CTAs per SM).  A
+// grid that runs in waves (B = 16: 2048 CTAs) takes five CTAs per SM (at
+// most 51 registers a thread), which keeps those waves at three.
+constexpr int kRecV32OneWave = 4;  // CTAs per SM of the unbounded form
+constexpr int kRecV32Waves = 5;
 
 // dv == 128, dk == DK (multiple of 8, <= 128).  Grid (Hv, batch), 256 threads.
 template <int DK>
@@ -140,8 +147,8 @@ __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v128(const Args a) {
 // four 128-byte row segments.  Row sums: per lane, then across the four row
 // lanes of a warp (shuffles), then across warps (shared memory).
 // Grid (Hv * dv / 32, batch), 256 threads; dk multiple of 32, <= 128.
-template <int DK>
-__global__ void __launch_bounds__(kRecWarps * 32) recurrent_v32(const Args a) {
+template <int DK, int MIN_CTAS>
+__global__ void __launch_bounds__(kRecWarps * 32, MIN_CTAS) recurrent_v32(const Args a) {
   constexpr int R = DK / 32;  // row passes per thread
   constexpr int DV = 128, kCols = 32;
   __shared__ float4 red_pred[kRecWarps][8];
@@ -157,6 +164,11 @@ __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v32(const Args a) {
   // prefetch never changes what a later load returns; one 128-byte row
   // segment per thread) and is loaded after the wait.
   auto row_of = [&](int p) { return warp * 4 + rs + 32 * p; };
+  // This CTA's key and query rows of token 0; the operands below keep the
+  // address arithmetic (a division by the group) ahead of the wait.
+  const float *k0 = a.k + size_t(seq) * a.tokens * a.key_heads * DK + size_t(kh) * DK;
+  const float *q0 = a.q + (k0 - a.k);
+  asm volatile("" ::"l"(k0), "l"(q0));
   float4 s[R];
   if (a.settled) {
 #pragma unroll
@@ -176,8 +188,8 @@ __global__ void __launch_bounds__(kRecWarps * 32) recurrent_v32(const Args a) {
   const size_t value_width = size_t(a.value_heads) * DV;
   for (uint32_t t = 0; t < a.tokens; ++t) {
     const size_t tok = size_t(seq) * a.tokens + t;
-    const float *kt = a.k + tok * key_width + size_t(kh) * DK;
-    const float *qt = a.q + tok * key_width + size_t(kh) * DK;
+    const float *kt = k0 + t * key_width;
+    const float *qt = q0 + t * key_width;
     const float dec = __ldg(a.decay + tok * a.value_heads + vh);
     const float bet = __ldg(a.beta + tok * a.value_heads + vh);
     const uint2 vraw = __ldg(reinterpret_cast<const uint2 *>(a.v + tok * value_width + vh * DV + col));

@@ -65,8 +65,10 @@ struct Partition {
   uint32_t prefetch_tiles;    // tiles a worker warms L2 with before it waits (<= 16)
 };
 
+// For a worker that holds records: its first tile, worker * tiles_per_worker,
+// lies below the tile count, which the plan keeps within 32 bits.
 __host__ __device__ inline uint32_t first_unit(const Partition &pt, uint32_t worker) {
-  return uint32_t((uint64_t(worker) * pt.tiles_per_worker) / pt.tiles_per_unit);
+  return worker * pt.tiles_per_worker / pt.tiles_per_unit;
 }
 
 __host__ __device__ inline uint64_t record_index(const Partition &pt, uint32_t worker,
@@ -336,13 +338,14 @@ __global__ void __launch_bounds__(RowShape<D, HKV, STAGES>::kThreads, 1)
     return;
   }
 
-  pdl_enter();  // before the queries are read
   // Consumer warp: kv head `warp`.
   const uint32_t h = warp;
   TileMath<D> math;
   uint32_t unit = 0xffffffffu;
   bool ok = true;
   uint32_t u = begin / tpu, key0 = (begin % tpu) * kTileKeys;  // tile t, advanced with t
+  asm volatile("" ::"r"(u), "r"(key0));  // the division stays ahead of the wait
+  pdl_enter();  // before the queries are read
   for (uint32_t t = begin; t < end; ++t) {
     const uint32_t j = t - begin;
     const int s = j % STAGES;
@@ -777,16 +780,22 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   const uint32_t G = a.group, D = a.head_dim;
   // This CTA's columns [d0, d1) of head_dim.
   const uint32_t slice = D / gridDim.y, d0 = blockIdx.y * slice, d1 = d0 + slice;
-  const uint32_t w_lo = uint32_t((uint64_t(unit) * pt.tiles_per_unit) / pt.tiles_per_worker);
-  const uint32_t w_hi =
-      uint32_t((uint64_t(unit + 1) * pt.tiles_per_unit - 1) / pt.tiles_per_worker);
+  // 32-bit partition arithmetic: the plan keeps the tile count within 32 bits
+  // (the host rejects more), so (unit + 1) * tiles_per_unit and the first
+  // tile of a worker that holds records both fit.
+  const uint32_t tpu = pt.tiles_per_unit, tpw = pt.tiles_per_worker;
+  const uint32_t w_lo = unit * tpu / tpw;
+  const uint32_t w_hi = ((unit + 1) * tpu - 1) / tpw;
   const uint32_t n = w_hi - w_lo + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Record i of the unit is worker w_lo + i's.  Every worker after w_lo
   // starts inside this unit (w * tiles_per_worker > unit * tiles_per_unit),
   // so its record is slot 0 of its span: the records from i = 1 on are
-  // evenly spaced, and only record 0 needs the general index.
-  const float *rec0 = a.records + record_index(pt, w_lo, unit, head) * a.record_floats;
+  // evenly spaced, and only record 0 needs the general index (slot
+  // unit - first_unit(w_lo)).
+  const uint32_t slot0 = unit - w_lo * tpw / tpu;
+  const float *rec0 =
+      a.records + ((uint64_t(w_lo) * pt.max_span + slot0) * pt.heads + head) * a.record_floats;
   const float *rec1 = a.records + (uint64_t(w_lo) * pt.max_span * pt.heads + head) * a.record_floats;
   const size_t rstep = size_t(pt.max_span) * pt.heads * a.record_floats;
   auto record = [&](uint32_t i) { return i == 0 ? rec0 : rec1 + i * rstep; };
@@ -801,21 +810,6 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   // instead of chaining a global load per record.
   __shared__ float staged[kMergeThreads / 32][2][kMergeSmemRecords];
   const bool stage = n <= uint32_t(kMergeSmemRecords);
-  wait_primary();
-  // The folded KvAppend: this CTA's share is columns [d0, d1) of kv head
-  // kvh of sequence seq's new K and V rows, loaded here and stored at the end
-  // (the load's latency hides under the merge).
-  const bool append = a.k_new != nullptr || a.v_new != nullptr;
-  const size_t new_at = seq * a.new_stride + size_t(kvh) * D;
-  const size_t cache_at = seq * a.cache_stride + (size_t(a.keys - 1) * a.kv_heads + kvh) * D;
-  __half k_row[kMergeAppendPerThread], v_row[kMergeAppendPerThread];
-#pragma unroll
-  for (int r = 0; r < kMergeAppendPerThread; ++r) {
-    const uint32_t d = d0 + threadIdx.x + r * kMergeThreads;
-    k_row[r] = append && a.k_new && d < d1 ? a.k_new[new_at + d] : __half();
-    v_row[r] = append && a.v_new && d < d1 ? a.v_new[new_at + d] : __half();
-  }
-  __half *out = a.out + (size_t(seq) * a.kv_heads * G + kvh * G) * D;
   // The slice's float4 columns, and the lane groups that sum interleaved
   // records (F a power of two below 32).
   const uint32_t F = (d1 - d0) / 4;
@@ -826,8 +820,38 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   // Few records (at most 4 per lane, kMergeHeld per lane group): one round
   // of loads fetches every max, sum and output column the warp needs, so
   // the merge costs one trip to the partial pass's records in L2 instead of
-  // one per dependent step.
+  // one per dependent step.  Its per-lane addresses: lane l's headers are
+  // records l + 32 s (hdr0 for s = 0, hdr1 + s * hstep after), lane group
+  // g's output columns records g + R j (col0 for j = 0, col1 + j * jstep
+  // after), the first `nj` of them valid.
   const bool one_round = grouped_lanes && n <= 128u && n <= R * uint32_t(kMergeHeld);
+  const float *hdr1 = rec1 + size_t(lane) * rstep;
+  const float *hdr0 = lane == 0 ? rec0 : hdr1;
+  const size_t hstep = 32 * rstep;
+  const float *col1 = rec1 + size_t(g) * rstep + 2 * G + 4 * (c0 + f);
+  const float *col0 = g == 0 ? rec0 + 2 * G + 4 * (c0 + f) : col1;
+  const size_t jstep = size_t(R) * rstep;
+  const uint32_t nj = g < n ? (n - g + R - 1) / R : 0u;
+  // Everything above depends only on the launch's arguments.  These operands
+  // make the compiler finish it before the wait, while the partial pass
+  // drains, instead of after it.
+  // The folded KvAppend: this CTA's share is columns [d0, d1) of kv head
+  // kvh of sequence seq's new K and V rows, loaded after the wait and stored
+  // at the end (the load's latency hides under the merge).
+  const bool append = a.k_new != nullptr || a.v_new != nullptr;
+  const size_t new_at = seq * a.new_stride + size_t(kvh) * D;
+  const size_t cache_at = seq * a.cache_stride + (size_t(a.keys - 1) * a.kv_heads + kvh) * D;
+  asm volatile("" ::"l"(hdr0), "l"(hdr1), "l"(col0), "l"(col1), "r"(nj), "r"(n), "l"(rstep),
+               "l"(new_at), "l"(cache_at));
+  wait_primary();
+  __half k_row[kMergeAppendPerThread], v_row[kMergeAppendPerThread];
+#pragma unroll
+  for (int r = 0; r < kMergeAppendPerThread; ++r) {
+    const uint32_t d = d0 + threadIdx.x + r * kMergeThreads;
+    k_row[r] = append && a.k_new && d < d1 ? a.k_new[new_at + d] : __half();
+    v_row[r] = append && a.v_new && d < d1 ? a.v_new[new_at + d] : __half();
+  }
+  __half *out = a.out + (size_t(seq) * a.kv_heads * G + kvh * G) * D;
   for (uint32_t h = warp; one_round && h < G; h += kMergeThreads / 32) {
     float *sm_w = staged[warp][0];
     float mv[4], lv[4];
@@ -835,15 +859,17 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
 #pragma unroll
     for (int s4 = 0; s4 < 4; ++s4) {
       const uint32_t i = lane + 32 * s4;
-      const float *r = record(min(i, n - 1));
-      mv[s4] = i < n ? r[h] : -INFINITY;
-      lv[s4] = i < n ? r[G + h] : 0.f;
+      // Past the unit's records the address stays on record 0 (in bounds).
+      const float *r = (s4 == 0 || i >= n ? hdr0 : hdr1 + s4 * hstep) + h;
+      mv[s4] = i < n ? r[0] : -INFINITY;
+      lv[s4] = i < n ? r[G] : 0.f;
     }
+    const size_t hd = size_t(h) * D;
 #pragma unroll
     for (int j = 0; j < kMergeHeld; ++j) {
-      const uint32_t i = g + R * j;
-      v[j] = i < n ? reinterpret_cast<const float4 *>(record(i) + 2 * G + h * D)[c0 + f]
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float *c = (j == 0 ? col0 : col1 + j * jstep) + hd;
+      v[j] = uint32_t(j) < nj ? *reinterpret_cast<const float4 *>(c)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float top = fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3]));
 #pragma unroll
@@ -866,8 +892,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int j = 0; j < kMergeHeld; ++j) {
-      const uint32_t i = g + R * j;
-      const float w = i < n ? sm_w[i] : 0.f;
+      const float w = uint32_t(j) < nj ? sm_w[g + R * j] : 0.f;
       acc.x = fmaf(v[j].x, w, acc.x);
       acc.y = fmaf(v[j].y, w, acc.y);
       acc.z = fmaf(v[j].z, w, acc.z);

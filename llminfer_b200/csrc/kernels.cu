@@ -1029,8 +1029,12 @@ int delta_update_impl(const llmi_delta_params *p, unsigned batch, const float *q
     // Fewer than four 128-column CTAs per SM: split the columns in four so
     // that the state streams through more CTAs at once.
     if (uint64_t(p->valueHeads) * batch < 4ull * uint64_t(dev.sm_count)) {
-      return launch_dependent("graphDeltaUpdate (recurrent, registers, 32-column blocks)",
-                              p->keyDim == 128 ? delta::recurrent_v32<128> : delta::recurrent_v32<64>,
+      const uint64_t ctas = uint64_t(p->valueHeads) * 4 * batch;
+      const bool one_wave = ctas <= uint64_t(delta::kRecV32OneWave) * dev.sm_count;
+      auto kernel = p->keyDim == 128
+                        ? (one_wave ? delta::recurrent_v32<128, delta::kRecV32OneWave> : delta::recurrent_v32<128, delta::kRecV32Waves>)
+                        : (one_wave ? delta::recurrent_v32<64, delta::kRecV32OneWave> : delta::recurrent_v32<64, delta::kRecV32Waves>);
+      return launch_dependent("graphDeltaUpdate (recurrent, registers, 32-column blocks)", kernel,
                               dim3(p->valueHeads * 4, batch), delta::kRecWarps * 32, 0, s, a);
     }
     return launch_dependent("graphDeltaUpdate (recurrent, registers)",
