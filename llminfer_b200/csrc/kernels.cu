@@ -1305,9 +1305,15 @@ extern "C" int llmi_cuda_delta_prepare(const llmi_delta_prep_params *p, unsigned
       return e;
     if (int e = ensure_silu_table(s, dev))
       return e;
-    const dim3 grid((p->tokens + producers::kPrepTokens - 1) / producers::kPrepTokens,
-                    (heads + 7) / 8, batch);
-    producers::delta_prepare_tiled<<<grid, 256, 0, s>>>(a);
+    if (int e = allow_smem(reinterpret_cast<const void *>(producers::delta_prepare_resident),
+                           producers::kPrepResidentSmem, dev))
+      return e;
+    const uint64_t tiles = (p->tokens + producers::kPrepTokens - 1) / producers::kPrepTokens;
+    const uint64_t warps = uint64_t(batch) * tiles * heads;
+    const uint64_t per_cta = producers::kPrepResidentThreads / 32;
+    const unsigned grid = unsigned(std::min<uint64_t>(dev.sm_count, (warps + per_cta - 1) / per_cta));
+    producers::delta_prepare_resident<<<grid, producers::kPrepResidentThreads,
+                                        producers::kPrepResidentSmem, s>>>(a);
   } else {
     const uint64_t rows = uint64_t(batch) * p->tokens * heads;
     producers::delta_prepare<<<grid_for(rows, 8), 256, 0, s>>>(a);

@@ -101,6 +101,7 @@ def test_causal_conv(batch, tokens, channels, k, silu):
 @pytest.mark.parametrize("batch,tokens,hk,hv", [
     (2, 1, 4, 8), (1, 3, 4, 8), (2, 70, 4, 8),
     (2, 40, 2, 5),   # 9 heads: the second group of 8 holds one
+    (2, 2000, 16, 32),  # the C5 heads: more (sequence, tile, head) items than resident warps
 ])
 def test_delta_prepare(batch, tokens, hk, hv):
     dk, dv, kern = 128, 128, 4
@@ -119,7 +120,8 @@ def test_delta_prepare(batch, tokens, hk, hv):
 
 def test_delta_prepare_silu_table_matches_computed_silu():
     # The tiled deltaPrepare takes half(silu(half(acc))) from a per-device
-    # fp16 table; the element-wise causalConv computes it.  The v channels of
+    # fp16 table (copied into shared memory); the element-wise causalConv
+    # computes it.  The v channels of
     # both must agree bit for bit over a wide range of conv outputs.
     batch, tokens, hk, dk, hv, dv, kern = 2, 50, 2, 128, 4, 128, 4
     width = 2 * hk * dk + hv * dv
