@@ -825,11 +825,12 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
   // g's output columns records g + R j (col0 for j = 0, col1 + j * jstep
   // after), the first `nj` of them valid.
   const bool one_round = grouped_lanes && n <= 128u && n <= R * uint32_t(kMergeHeld);
+  // Addresses of records past the unit's last stay on record 0 (in bounds).
   const float *hdr1 = rec1 + size_t(lane) * rstep;
-  const float *hdr0 = lane == 0 ? rec0 : hdr1;
+  const float *hdr0 = lane == 0 || uint32_t(lane) >= n ? rec0 : hdr1;
   const size_t hstep = 32 * rstep;
   const float *col1 = rec1 + size_t(g) * rstep + 2 * G + 4 * (c0 + f);
-  const float *col0 = g == 0 ? rec0 + 2 * G + 4 * (c0 + f) : col1;
+  const float *col0 = g == 0 || g >= n ? rec0 + 2 * G + 4 * (c0 + f) : col1;
   const size_t jstep = size_t(R) * rstep;
   const uint32_t nj = g < n ? (n - g + R - 1) / R : 0u;
   // Everything above depends only on the launch's arguments.  These operands
@@ -859,7 +860,6 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
 #pragma unroll
     for (int s4 = 0; s4 < 4; ++s4) {
       const uint32_t i = lane + 32 * s4;
-      // Past the unit's records the address stays on record 0 (in bounds).
       const float *r = (s4 == 0 || i >= n ? hdr0 : hdr1 + s4 * hstep) + h;
       mv[s4] = i < n ? r[0] : -INFINITY;
       lv[s4] = i < n ? r[G] : 0.f;
