@@ -137,6 +137,54 @@ def test_partition_invariance():
     b.close()
 
 
+def test_decode_steps_agree_however_they_are_issued():
+    # The session passes LLMI_FLAG_SETTLED to its decode-path calls only when
+    # its earlier steps are known complete: after a synchronising step, and
+    # for the first step of each stream capture, not for a step enqueued
+    # behind an unsynchronised one.  The three ways of issuing the same decode
+    # steps must give the same bits (outputs, caches and states).
+    batch, capacity, prefill, steps = 2, 64, 20, 4
+    pre = [make_inputs(batch, prefill, l, seed=90) for l in range(len(KINDS))]
+    dec = [[make_inputs(batch, 1, l, seed=91 + i) for l in range(len(KINDS))]
+           for i in range(steps)]
+    results = {}
+    for mode in ("step", "enqueue", "graphs"):
+        session = ops.AttentionSession(KINDS, batch, capacity, **SHAPE)
+        session.step(prefill, [to_layer(x) for x in pre])
+        layers = [[to_layer(x) for x in d] for d in dec]
+        torch.cuda.synchronize()
+        if mode == "step":
+            for step_layers in layers:
+                session.step(1, step_layers)
+        elif mode == "enqueue":
+            for step_layers in layers:
+                session.enqueue(1, step_layers)
+            session.sync()
+        else:
+            graphs = []
+            for step_layers in layers:
+                table = session.operand_table(step_layers)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=session.stream):
+                    session.enqueue(1, table)
+                graphs.append((g, table))
+            for g, _ in graphs:
+                g.replay()
+            torch.cuda.synchronize()
+            session.sync()
+            del graphs
+        assert session.past == prefill + steps
+        outs = [x.out.clone() for step_layers in layers for x in step_layers]
+        states = [session.read_state(l, abi.STATE_RECURRENT if k == abi.LAYER_DELTANET
+                                     else abi.STATE_KEYS).clone() for l, k in enumerate(KINDS)]
+        results[mode] = (outs, states)
+        session.close()
+    for mode in ("enqueue", "graphs"):
+        for a, b in zip(results["step"][0] + results["step"][1],
+                        results[mode][0] + results[mode][1]):
+            assert torch.equal(a.view(torch.uint8), b.view(torch.uint8)), mode
+
+
 PRODUCER_KINDS = [abi.LAYER_DELTANET, abi.LAYER_GQA]
 
 
