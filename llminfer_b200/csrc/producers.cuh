@@ -80,6 +80,9 @@ struct RopeArgs {
 // rows (uint4 loads and stores).
 constexpr int kRopeMaxRotary = 256;  // rotary dims (Qwen3.5 rotates 64)
 constexpr int kRopeMaxPairs = kRopeMaxRotary / 2;
+// Head rows in flight per warp (head_dim <= 256): at the C5 shape 1 took
+// 0.603 ms, 3 0.576 ms, 4 0.586 ms (a few registers spilled).
+constexpr int kRopeAhead = 3;
 template <bool kVec, int kChunks = 1>
 __global__ void __launch_bounds__(32 * kRopeWarps, kChunks == 1 ? 4 : 2)
     norm_rope(const RopeArgs a) {
@@ -111,8 +114,12 @@ __global__ void __launch_bounds__(32 * kRopeWarps, kChunks == 1 ? 4 : 2)
   };
   if constexpr (kVec) {
     // Lane l holds elements 8l + 256k .. +8 (k < kChunks, head_dim <= 256
-    // kChunks) of every row in registers, with (1 + w) for them; the next
-    // head's row is loaded while this one is processed.
+    // kChunks) of every row in registers, with (1 + w) for them.  The rows of
+    // the next kAhead - 1 heads are in flight while one is processed: a ring
+    // of kAhead rows, slot u refilled with head h + kAhead as soon as head h
+    // has been copied out of it (one row ahead left each SM about 16 KB of
+    // loads in flight, far below what HBM latency needs).
+    constexpr int kAhead = kChunks == 1 ? kRopeAhead : 2;
     float wp1[kChunks][8];
 #pragma unroll
     for (int k = 0; k < kChunks; ++k)
@@ -121,7 +128,7 @@ __global__ void __launch_bounds__(32 * kRopeWarps, kChunks == 1 ? 4 : 2)
         const unsigned i = 256 * k + 8 * lane + e;
         wp1[k][e] = (a.weight && i < D) ? 1.0f + a.weight[i] : 1.0f;
       }
-    uint4 cur[kChunks], nxt[kChunks];
+    uint4 ring[kAhead][kChunks];
     auto load = [&](unsigned h, uint4 (&r)[kChunks]) {
       const __half *in = row_in(h);
 #pragma unroll
@@ -129,64 +136,71 @@ __global__ void __launch_bounds__(32 * kRopeWarps, kChunks == 1 ? 4 : 2)
         if (256 * k + 8 * lane < D)
           r[k] = *reinterpret_cast<const uint4 *>(in + 256 * k + 8 * lane);
     };
-    load(0, cur);
-    for (unsigned h = 0; h < a.heads; ++h) {
-      if (h + 1 < a.heads)
-        load(h + 1, nxt);
-      float scale = 1.f;
-      if (a.weight) {
-        float sum = 0.f;
+#pragma unroll
+    for (int u = 0; u < kAhead; ++u)
+      if (unsigned(u) < a.heads)
+        load(u, ring[u]);
+    for (unsigned h0 = 0; h0 < a.heads; h0 += kAhead) {
+#pragma unroll
+      for (int u = 0; u < kAhead; ++u) {
+        const unsigned h = h0 + u;
+        if (h >= a.heads)
+          break;
+        uint4 (&cur)[kChunks] = ring[u];
+        float scale = 1.f;
+        if (a.weight) {
+          float sum = 0.f;
+#pragma unroll
+          for (int k = 0; k < kChunks; ++k)
+            if (256 * k + 8 * lane < D) {
+              const __half *hv = reinterpret_cast<const __half *>(&cur[k]);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float v = __half2float(hv[e]);
+                sum = fmaf(v, v, sum);
+              }
+            }
+          sum = warp_sum(sum);
+          scale = rsqrtf(sum / float(D) + a.epsilon);
+        }
 #pragma unroll
         for (int k = 0; k < kChunks; ++k)
           if (256 * k + 8 * lane < D) {
-            const __half *hv = reinterpret_cast<const __half *>(&cur[k]);
+            uint4 o = cur[k];
+            if (a.weight) {
+              const __half *hv = reinterpret_cast<const __half *>(&cur[k]);
+              float v[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float v = __half2float(hv[e]);
-              sum = fmaf(v, v, sum);
+              for (int e = 0; e < 8; ++e)
+                v[e] = __half2float(hv[e]) * scale * wp1[k][e];
+              o = make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]),
+                             pack_half2(v[4], v[5]), pack_half2(v[6], v[7]));
             }
+            *reinterpret_cast<uint4 *>(x + 256 * k + 8 * lane) = o;
           }
-        sum = warp_sum(sum);
-        scale = rsqrtf(sum / float(D) + a.epsilon);
-      }
+        if (h + kAhead < a.heads)
+          load(h + kAhead, cur);
+        __syncwarp();
 #pragma unroll
-      for (int k = 0; k < kChunks; ++k)
-        if (256 * k + 8 * lane < D) {
-          uint4 o = cur[k];
-          if (a.weight) {
-            const __half *hv = reinterpret_cast<const __half *>(&cur[k]);
-            float v[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              v[e] = __half2float(hv[e]) * scale * wp1[k][e];
-            o = make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]),
-                           pack_half2(v[4], v[5]), pack_half2(v[6], v[7]));
+        for (int k = 0; k < kPerLane; ++k) {
+          const unsigned i = lane + 32 * k;
+          if (i < half_r) {
+            const unsigned j = i + half_r;
+            const float xv = __half2float(x[i]), yv = __half2float(x[j]);
+            x[i] = __float2half_rn(round_half(xv * cs[k]) - round_half(yv * sn[k]));
+            x[j] = __float2half_rn(round_half(yv * cs[k]) + round_half(xv * sn[k]));
           }
-          *reinterpret_cast<uint4 *>(x + 256 * k + 8 * lane) = o;
         }
-      __syncwarp();
+        __syncwarp();
+        __half *out = a.output + seq * a.output_stride +
+                      (uint64_t(a.output_start) * a.heads + uint64_t(token) * a.heads + h) * D;
 #pragma unroll
-      for (int k = 0; k < kPerLane; ++k) {
-        const unsigned i = lane + 32 * k;
-        if (i < half_r) {
-          const unsigned j = i + half_r;
-          const float xv = __half2float(x[i]), yv = __half2float(x[j]);
-          x[i] = __float2half_rn(round_half(xv * cs[k]) - round_half(yv * sn[k]));
-          x[j] = __float2half_rn(round_half(yv * cs[k]) + round_half(xv * sn[k]));
-        }
+        for (int k = 0; k < kChunks; ++k)
+          if (256 * k + 8 * lane < D)
+            *reinterpret_cast<uint4 *>(out + 256 * k + 8 * lane) =
+                *reinterpret_cast<const uint4 *>(x + 256 * k + 8 * lane);
+        __syncwarp();  // the row buffer is reused by the next head
       }
-      __syncwarp();
-      __half *out = a.output + seq * a.output_stride +
-                    (uint64_t(a.output_start) * a.heads + uint64_t(token) * a.heads + h) * D;
-#pragma unroll
-      for (int k = 0; k < kChunks; ++k)
-        if (256 * k + 8 * lane < D)
-          *reinterpret_cast<uint4 *>(out + 256 * k + 8 * lane) =
-              *reinterpret_cast<const uint4 *>(x + 256 * k + 8 * lane);
-      __syncwarp();  // the row buffer is reused by the next head
-#pragma unroll
-      for (int k = 0; k < kChunks; ++k)
-        cur[k] = nxt[k];
     }
   } else {
   for (unsigned h = 0; h < a.heads; ++h) {
