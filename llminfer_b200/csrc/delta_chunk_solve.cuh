@@ -27,7 +27,7 @@
 // Warp MMAs (m16n8k16, fp16 in, fp32 accumulation) do k k^T and the blocked
 // substitution; the 16x16 diagonal blocks are inverted by forward
 // substitution in fp32.  A 128-thread CTA holds no tensor memory and about
-// 42 KB of shared memory, so several run on each SM.
+// 35 KB of shared memory and 80 registers, so six run on each SM.
 #pragma once
 
 #include "common.cuh"
@@ -47,14 +47,20 @@ constexpr uint32_t kImageBytes = C * C * 2;     // one Tu image
 constexpr uint32_t kKImageBytes = C * DK * 2;   // one chunk's k rows
 
 struct Smem {
-  __half k[C * kLdK];       // k rows of the chunk, fp16
+  // The k rows are read only up to k k^T, which every warp finishes before
+  // the first barrier of the value-head loop; the Tu image, written two
+  // barriers later, takes their place.  35 KB in all: six CTAs per SM.
+  union {
+    __half k[C * kLdK];                    // k rows of the chunk, fp16
+    alignas(128) uint8_t tu[kImageBytes];  // the Tu image
+  };
   __half am[C * kLdA];      // A, fp16 (blocks below the diagonal are read)
   float ad[4 * 16 * 16];    // diagonal blocks of A, fp32, [block][s][t]
   __half td[C * kLdT];      // inverses of the diagonal blocks of I + A, fp16
   float g2[kMaxGroup][C];   // per value head of the key head: G_t in log2 units
   float bet[kMaxGroup][C];  // beta_t (0 past the last token)
-  alignas(128) uint8_t tu[kImageBytes];  // the Tu image
 };
+static_assert(sizeof(Smem) + 1024 <= 232448 / 6, "six solve CTAs per SM");
 
 // One 16x16 fp16 tile of a row-major array as an m16n8k16 A fragment.
 __device__ __forceinline__ void frag_a(uint32_t (&f)[4], const __half *base, int ld, int m0,
@@ -65,7 +71,7 @@ __device__ __forceinline__ void frag_a(uint32_t (&f)[4], const __half *base, int
 // Grid (chunks, key heads, batch), kThreads threads, sizeof(Smem) bytes of
 // dynamic shared memory.  tu_out: [batch][value heads][chunks] Tu images;
 // k_out: [batch][key heads][chunks] k-row images.
-__global__ void __launch_bounds__(kThreads, 5)
+__global__ void __launch_bounds__(kThreads, 6)
     solve_pass(const delta::Args a, uint8_t *__restrict__ tu_out, uint8_t *__restrict__ k_out) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
