@@ -865,11 +865,14 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
       lv[s4] = i < n ? r[G] : 0.f;
     }
     const size_t hd = size_t(h) * D;
+    // Only the lane group's nj records: the loops below stop there instead
+    // of issuing the rest predicated off.
 #pragma unroll
     for (int j = 0; j < kMergeHeld; ++j) {
+      if (uint32_t(j) >= nj)
+        break;
       const float *c = (j == 0 ? col0 : col1 + j * jstep) + hd;
-      v[j] = uint32_t(j) < nj ? *reinterpret_cast<const float4 *>(c)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[j] = *reinterpret_cast<const float4 *>(c);
     }
     float top = fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3]));
 #pragma unroll
@@ -892,7 +895,9 @@ __global__ void __launch_bounds__(kMergeThreads) merge(const Args a) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int j = 0; j < kMergeHeld; ++j) {
-      const float w = uint32_t(j) < nj ? sm_w[g + R * j] : 0.f;
+      if (uint32_t(j) >= nj)
+        break;
+      const float w = sm_w[g + R * j];
       acc.x = fmaf(v[j].x, w, acc.x);
       acc.y = fmaf(v[j].y, w, acc.y);
       acc.z = fmaf(v[j].z, w, acc.z);
